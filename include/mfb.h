@@ -1,0 +1,175 @@
+/*
+ * mfb.h — C ABI of the B200 (sm_100a) dense FP32 contraction library (libmfb.so).
+ *
+ * Every entry point takes plain pointers, sizes and a CUDA stream handle; no C++
+ * or framework types cross this boundary. All matrices are row-major FP32 with
+ * explicit leading dimensions (elements), exactly like the reference's pointer
+ * interface. Buffers are caller-owned device memory unless stated otherwise.
+ *
+ * Replaces (reference file:line):
+ *   mfb_cuda_gemm / mfb_cuda_sync   matrix_pro::hw::cuda_gemm / cuda_sync
+ *                                   include/matrix_pro/detail/cuda_hooks.hpp:17-18,28
+ *                                   (body: src/hw/cuda_backend.cu:91-99,159-163)
+ *   mfb_sgemm                       the cublasLtMatmul/cublasGemmEx call of GemmPlan::Impl::run_ptr
+ *                                   src/ops/gemm/plan/implementation.inc:128-151
+ *   mfb_plan_*                      GemmPlan ctor/execute/tune/rows/cols/inner/candidate_count
+ *                                   include/matrix_pro/ops/gemm.hpp:36-62
+ *                                   (src/ops/gemm/plan/implementation.inc:5-152, tuning.inc:5-66)
+ *   mfb_gemv                        gemm_gemv (gemv_rows_kernel, gemm_skinny_n_kernel, gemv_cols_kernel)
+ *                                   src/ops/gemm/gemm_gemv.cu:86-110
+ *   mfb_conv2d_fwd                  matrix_pro::conv2d  include/matrix_pro/nn/conv.hpp:16-17
+ *                                   (src/nn/conv.cu:110-163)
+ *   mfb_naive_sgemm                 the one-thread-per-output comparison GEMM
+ *                                   benchmarks/bench_comparison.cu:76 (device correctness oracle)
+ */
+#ifndef MFB_H_
+#define MFB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define MFB_API __declspec(dllexport)
+#else
+#define MFB_API __attribute__((visibility("default")))
+#endif
+
+/* Same handle type as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* mfb_stream_t;
+
+typedef enum mfb_status_t {
+    MFB_OK = 0,
+    MFB_EINVAL = 1,        /* bad argument: shape, stride, alias, pointer, option */
+    MFB_ECUDA = 2,         /* a CUDA runtime/driver call failed (message: mfb_last_error) */
+    MFB_ETIMEOUT = 3,      /* a bounded device-side wait gave up (see mfb_device_status) */
+    MFB_ENCCL = 4,         /* an NCCL call failed */
+    MFB_EUNSUPPORTED = 5,  /* valid request this build cannot serve (e.g. no sm_100 device) */
+    MFB_ENOMEM = 6,        /* workspace allocation failed */
+    MFB_ESHAPE = 7         /* operand shapes disagree (the reference's ShapeMismatchError) */
+} mfb_status_t;
+
+typedef enum mfb_precision_t {
+    MFB_PRECISION_FP32 = 0, /* strict FP32 (default): error-compensated 3xTF32 on tcgen05 */
+    MFB_PRECISION_TF32 = 1  /* single-pass TF32 inputs, FP32 accumulation */
+} mfb_precision_t;
+
+typedef enum mfb_epilogue_t {
+    MFB_EPILOGUE_NONE = 0,
+    MFB_EPILOGUE_BIAS = 1,      /* + bias[col] */
+    MFB_EPILOGUE_BIAS_RELU = 2, /* relu(. + bias[col]) */
+    MFB_EPILOGUE_BIAS_GELU = 3  /* tanh-GELU(. + bias[col]) */
+} mfb_epilogue_t;
+
+/*
+ * C[m x n] = epilogue(alpha * op(A) * op(B) + beta * C).
+ * op(A) is m x k: A is stored m x k (lda >= k) or, with trans_a, k x m (lda >= m).
+ * op(B) is k x n: B is stored k x n (ldb >= n) or, with trans_b, n x k (ldb >= k).
+ * ldc >= n. beta == 0 never reads C. k == 0 or alpha == 0 gives C = beta * C
+ * followed by the epilogue (reference: implementation.inc:133-149).
+ */
+typedef struct mfb_gemm_desc {
+    int m, n, k;
+    int lda, ldb, ldc;
+    float alpha, beta;
+    int precision; /* mfb_precision_t */
+    int trans_a, trans_b;
+    int epilogue; /* mfb_epilogue_t */
+} mfb_gemm_desc;
+
+/* ---------------------------------------------------------------- status & errors */
+MFB_API const char* mfb_status_string(mfb_status_t status);
+/* Detail text of the last failure on the calling thread ("" when none). */
+MFB_API const char* mfb_last_error(void);
+/* Library version string and the kernel families compiled in. */
+MFB_API const char* mfb_version(void);
+
+/* Reads and clears the device status word that bounded waits report into.
+ * *bits receives the raw word (0 = no timeout since the last read). Synchronizes
+ * the device first. Returns MFB_ETIMEOUT when any bit was set. */
+MFB_API mfb_status_t mfb_device_status(int device, uint32_t* bits);
+/* Bound, in nanoseconds of device time, for every device-side wait of later launches
+ * (default 4e9 = 4 s). Process-wide. */
+MFB_API mfb_status_t mfb_set_wait_limit_ns(uint64_t limit_ns);
+MFB_API uint64_t mfb_get_wait_limit_ns(void);
+/* Synchronizes `stream` on `device`, then reports CUDA errors and device timeouts. */
+MFB_API mfb_status_t mfb_sync(int device, mfb_stream_t stream);
+
+/* ---------------------------------------------------------------- hw::cuda_gemm drop-in */
+/* Asynchronous strict-FP32 GEMM on the device's internal stream (created lazily),
+ * thread-safe through a per-device lock; wait with mfb_cuda_sync. Same arguments
+ * and meaning as matrix_pro::hw::cuda_gemm (cuda_hooks.hpp:17-18). */
+MFB_API mfb_status_t mfb_cuda_gemm(int device, int m, int n, int k, const float* a, int lda, const float* b,
+                                   int ldb, float* c, int ldc, float alpha, float beta);
+MFB_API mfb_status_t mfb_cuda_sync(int device);
+MFB_API mfb_status_t mfb_cuda_device_count(int* count);
+
+/* ---------------------------------------------------------------- one-shot GEMM */
+/* Stream-ordered GEMM. Scratch (3xTF32 split planes, repacked operands) comes from a
+ * per-(device, stream) cache that grows on demand; for allocation-free launches
+ * (CUDA graph capture) create a plan. bias: n floats, required iff epilogue != NONE. */
+MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
+                               const float* b, float* c, const float* bias);
+
+/* ---------------------------------------------------------------- plans */
+typedef struct mfb_plan* mfb_plan_t;
+
+typedef struct mfb_plan_info {
+    int m, n, k;
+    int precision, trans_a, trans_b, epilogue;
+    int path;              /* 0 tcgen05 GEMM, 1 GEMV/skinny, 2 scale-only (k == 0), 3 empty (m or n == 0) */
+    int tile_n;            /* tcgen05 tile width (128 x tile_n) */
+    int stages;            /* shared-memory pipeline depth */
+    int candidates;        /* tile configurations considered by mfb_plan_tune */
+    size_t workspace_bytes;/* device scratch owned by the plan */
+    char kernel[64];       /* kernel family name */
+} mfb_plan_info;
+
+/* Builds tile choice, scratch and launch state for one problem on `device`.
+ * Allocates all scratch now; execute allocates nothing and is graph-capturable.
+ * desc->alpha/beta are ignored (they are execute arguments). */
+MFB_API mfb_status_t mfb_plan_create(int device, const mfb_gemm_desc* desc, mfb_plan_t* out);
+MFB_API mfb_status_t mfb_plan_execute(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
+                                      float* c, float alpha, float beta, const float* bias);
+/* Times every admissible tile configuration on `scratch_c` (an m x n buffer with ldc
+ * of the plan; c is never touched), keeps the fastest, and reports it. Synchronizes. */
+MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
+                                   float* scratch_c, int repeats, int* candidates_tested, float* best_ms);
+MFB_API mfb_status_t mfb_plan_info_get(mfb_plan_t plan, mfb_plan_info* info);
+MFB_API mfb_status_t mfb_plan_destroy(mfb_plan_t plan);
+
+/* ---------------------------------------------------------------- GEMV / skinny */
+/* Bandwidth-bound FP32 kernel for n <= 16 (y = A x with ldb/ldc strides) and for
+ * m == 1 (row vector times matrix). Strict FP32 FMA arithmetic; trans_a/trans_b must
+ * be 0. alpha/beta/epilogue as mfb_sgemm. */
+MFB_API mfb_status_t mfb_gemv(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
+                              const float* b, float* c, const float* bias);
+
+/* ---------------------------------------------------------------- conv2d forward */
+/* NCHW cross-correlation: x (N,C,H,W), w (K,C,R,S), bias (K), y (N,K,P,Q) with
+ * P = (H + 2 pad - R) / stride + 1, Q = (W + 2 pad - S) / stride + 1.
+ * precision as mfb_precision_t. Scratch from the per-(device, stream) cache. */
+MFB_API mfb_status_t mfb_conv2d_fwd(int device, mfb_stream_t stream, int n, int c, int h, int w, int k, int r,
+                                    int s, int stride, int pad, const float* x, const float* wgt,
+                                    const float* bias, float* y, int precision);
+
+/* ---------------------------------------------------------------- device oracle */
+/* One thread per output, FP32 FMA chain over k in order: a slow correctness oracle
+ * that runs on the device (same desc semantics, no transposes). */
+MFB_API mfb_status_t mfb_naive_sgemm(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
+                                     const float* b, float* c, const float* bias);
+
+/* ---------------------------------------------------------------- failure-path probe */
+/* Launches a kernel that waits on an mbarrier nothing arrives on, bounded by
+ * limit_ns; it records kStatusTimeoutProbe in the status word and returns. Used by
+ * tests to exercise the timeout path without faulting or hanging the GPU. */
+MFB_API mfb_status_t mfb_probe_wait_timeout(int device, mfb_stream_t stream, uint64_t limit_ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MFB_H_ */

@@ -1,0 +1,351 @@
+// Host side of the tcgen05 GEMM: operand preparation (3xTF32 split planes or
+// repacking of operands TMA cannot address in place), TMA descriptor encoding,
+// tile-configuration choice and launch. The reference's cuBLAS/cuBLASLt bodies
+// this replaces: src/hw/cuda_backend.cu:91-99 and
+// src/ops/gemm/plan/implementation.inc:111-151.
+#include "gemm_tc.cuh"
+#include "mfb_internal.h"
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+namespace mfb {
+
+// ------------------------------------------------------------------------------------
+// Prepass kernels (HBM-bound, 128-bit accesses where the layout allows)
+// ------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float round_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// hi = tf32(x) (round to nearest), lo = tf32(x - hi); x - hi is exact in FP32, so
+// hi + lo carries 22 significant bits of x. lo == nullptr copies x unchanged into hi
+// (repacking to a TMA-addressable layout, used by the TF32 mode).
+__global__ void split_tf32_kernel(const float* __restrict__ x, long long ldx, int rows, int cols,
+                                  float* __restrict__ hi, float* __restrict__ lo, long long ldp, int vec_in) {
+    const long long groups_per_row = ldp / 4;
+    const long long total = static_cast<long long>(rows) * groups_per_row;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = idx / groups_per_row;
+        const int c0 = static_cast<int>(idx - r * groups_per_row) * 4;
+        const float* src = x + r * ldx + c0;
+        float v[4];
+        if (vec_in && c0 + 3 < cols) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(src));
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = (c0 + j < cols) ? __ldg(src + j) : 0.0f;
+        }
+        float4 h, l;
+        if (lo != nullptr) {
+            float hv[4], lv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                hv[j] = round_tf32(v[j]);
+                lv[j] = round_tf32(v[j] - hv[j]);
+            }
+            h = make_float4(hv[0], hv[1], hv[2], hv[3]);
+            l = make_float4(lv[0], lv[1], lv[2], lv[3]);
+            *reinterpret_cast<float4*>(lo + r * ldp + c0) = l;
+        } else {
+            h = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        *reinterpret_cast<float4*>(hi + r * ldp + c0) = h;
+    }
+}
+
+// C = beta * C (beta == 0 writes zeros without reading), then the column-bias epilogue.
+// Mirrors scale_output + apply_epilogue of the reference (plan/epilogue.cuh:20,
+// gemm_fused.cu:23-60) for the k == 0 / alpha == 0 case.
+__global__ void scale_epilogue_kernel(float* __restrict__ c, long long ldc, int m, int n, float beta,
+                                      const float* __restrict__ bias, int epilogue) {
+    const long long total = static_cast<long long>(m) * n;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = idx / n;
+        const int col = static_cast<int>(idx - r * n);
+        float* p = c + r * ldc + col;
+        const float v = beta == 0.0f ? 0.0f : beta * *p;
+        *p = apply_epilogue_op(v, bias, col, epilogue);
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// TMA descriptors
+// ------------------------------------------------------------------------------------
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// 3-D map over a stored row-major matrix (cols contiguous) with an outer plane axis.
+// K-major tiles use the 128B swizzle with 16-byte atoms; MN-major TF32 tiles the 128B
+// swizzle with 32-byte atoms, the only shared-memory layout tcgen05 accepts for them.
+mfb_status_t encode_operand(CUtensorMap* map, const float* base, int rows, int cols, long long ld, int planes,
+                            long long plane_stride_floats, int box_cols, int box_rows, bool mn_major) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(MFB_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(planes)};
+    long long plane_stride = plane_stride_floats > 0 ? plane_stride_floats : ld * static_cast<long long>(rows);
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(plane_stride) * 4};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows),
+                               static_cast<cuuint32_t>(planes)};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(MFB_ECUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
+    return MFB_OK;
+}
+
+// ------------------------------------------------------------------------------------
+// Kernel table
+// ------------------------------------------------------------------------------------
+using TcKernel = void (*)(CUtensorMap, CUtensorMap, GemmTcParams);
+
+struct TcEntry {
+    int bn, stages, planes, a_mn, b_mn;
+    const void* fn;
+    int smem;
+};
+
+template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
+TcEntry make_entry() {
+    return TcEntry{BN, STAGES, PLANES, A_MN, B_MN,
+                   reinterpret_cast<const void*>(&gemm_tf32_tc_kernel<BN, STAGES, PLANES, A_MN, B_MN>),
+                   GemmTcSmem<BN, STAGES, PLANES>::kBytes};
+}
+
+const TcEntry* kernel_table(int* count) {
+    static const TcEntry table[] = {
+        // strict FP32 (3xTF32 split planes, chunked round-to-nearest accumulation)
+        make_entry<128, 3, 2, 0, 1>(),
+        make_entry<128, 3, 2, 1, 1>(),
+        make_entry<128, 3, 2, 0, 0>(),
+        make_entry<128, 3, 2, 1, 0>(),
+        // TF32 single pass
+        make_entry<256, 4, 1, 0, 1>(),
+        make_entry<128, 6, 1, 0, 1>(),
+        make_entry<64, 8, 1, 0, 1>(),
+        make_entry<128, 6, 1, 1, 1>(),
+        make_entry<128, 6, 1, 0, 0>(),
+        make_entry<128, 6, 1, 1, 0>(),
+    };
+    *count = static_cast<int>(sizeof(table) / sizeof(table[0]));
+    return table;
+}
+
+const TcEntry* find_kernel(const TcConfig& c) {
+    int count = 0;
+    const TcEntry* t = kernel_table(&count);
+    for (int i = 0; i < count; ++i)
+        if (t[i].bn == c.bn && t[i].stages == c.stages && t[i].planes == c.planes && t[i].a_mn == c.a_mn &&
+            t[i].b_mn == c.b_mn)
+            return &t[i];
+    return nullptr;
+}
+
+long long round_up(long long v, long long q) { return (v + q - 1) / q * q; }
+
+struct PreparedOperand {
+    const float* base = nullptr;
+    int rows = 0, cols = 0;
+    long long ld = 0;
+    long long plane_stride = 0;  // floats; 0 when one plane
+    bool needs_prepass = false;
+};
+
+// Stored-matrix geometry of op(A) / op(B).
+void stored_dims(const mfb_gemm_desc& d, bool is_a, int* rows, int* cols, long long* ld) {
+    if (is_a) {
+        *rows = d.trans_a ? d.k : d.m;
+        *cols = d.trans_a ? d.m : d.k;
+        *ld = d.lda;
+    } else {
+        *rows = d.trans_b ? d.n : d.k;
+        *cols = d.trans_b ? d.k : d.n;
+        *ld = d.ldb;
+    }
+}
+
+size_t plane_floats(int rows, int cols) {
+    return static_cast<size_t>(round_up(static_cast<long long>(rows) * round_up(cols, 4), 64));
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------
+// Configuration choice
+// ------------------------------------------------------------------------------------
+int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
+    const int planes = d.precision == MFB_PRECISION_TF32 ? 1 : 2;
+    const int a_mn = d.trans_a ? 1 : 0;
+    const int b_mn = d.trans_b ? 0 : 1;
+    int count = 0;
+    const TcEntry* t = kernel_table(&count);
+    const int sms = 148;
+    const long long tiles_m = (d.m + kBM - 1) / kBM;
+    // Widest tile that still fills the GPU goes first; the rest follow by width.
+    int order[16];
+    int n_ok = 0;
+    for (int i = 0; i < count && n_ok < 16; ++i)
+        if (t[i].planes == planes && t[i].a_mn == a_mn && t[i].b_mn == b_mn) order[n_ok++] = i;
+    std::sort(order, order + n_ok, [&](int x, int y) {
+        auto score = [&](int idx) {
+            const long long tiles = tiles_m * ((d.n + t[idx].bn - 1) / t[idx].bn);
+            const bool fills = tiles >= (sms * 4) / 5;
+            return (fills ? 1000 : 0) + (fills ? t[idx].bn : -t[idx].bn);
+        };
+        return score(x) > score(y);
+    });
+    int n_out = 0;
+    for (int i = 0; i < n_ok && n_out < max_out; ++i) {
+        TcConfig c;
+        c.bn = t[order[i]].bn;
+        c.stages = t[order[i]].stages;
+        c.planes = planes;
+        c.a_mn = a_mn;
+        c.b_mn = b_mn;
+        out[n_out++] = c;
+    }
+    return n_out;
+}
+
+size_t tc_workspace_bytes(const mfb_gemm_desc& d, const float* a, const float* b, bool assume_aligned_inputs) {
+    size_t bytes = 0;
+    for (int which = 0; which < 2; ++which) {
+        int rows, cols;
+        long long ld;
+        stored_dims(d, which == 0, &rows, &cols, &ld);
+        const float* p = which == 0 ? a : b;
+        if (d.precision == MFB_PRECISION_TF32) {
+            const bool in_place = (ld % 4 == 0) && (assume_aligned_inputs || aligned16(p));
+            if (!in_place) bytes += plane_floats(rows, cols) * 4;
+        } else {
+            bytes += 2 * plane_floats(rows, cols) * 4;
+        }
+    }
+    return bytes;
+}
+
+mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c, const float* bias) {
+    const long long total = static_cast<long long>(d.m) * d.n;
+    if (total == 0) return MFB_OK;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    scale_epilogue_kernel<<<blocks, 256, 0, stream>>>(c, d.ldc, d.m, d.n, d.beta, bias, d.epilogue);
+    MFB_CUDA_TRY(cudaGetLastError(), "scale/epilogue launch");
+    return MFB_OK;
+}
+
+mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
+                     const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes) {
+    const TcEntry* e = find_kernel(cfg);
+    if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 kernel for this tile configuration");
+
+    // --- operand preparation: split planes (strict) or repack (TF32, unaligned) ---
+    PreparedOperand ops[2];
+    size_t used = 0;
+    char* ws = static_cast<char*>(workspace);
+    for (int which = 0; which < 2; ++which) {
+        PreparedOperand& op = ops[which];
+        long long ld;
+        stored_dims(d, which == 0, &op.rows, &op.cols, &ld);
+        const float* src = which == 0 ? a : b;
+        const bool in_place = cfg.planes == 1 && (ld % 4 == 0) && aligned16(src);
+        if (in_place) {
+            op.base = src;
+            op.ld = ld;
+            continue;
+        }
+        const long long ldp = round_up(op.cols, 4);
+        const size_t pf = plane_floats(op.rows, op.cols);
+        const size_t need = pf * 4 * static_cast<size_t>(cfg.planes);
+        if (used + need > workspace_bytes || ws == nullptr)
+            return fail(MFB_EINVAL, "workspace too small for the tcgen05 operand planes");
+        float* hi = reinterpret_cast<float*>(ws + used);
+        float* lo = cfg.planes == 2 ? hi + pf : nullptr;
+        used += need;
+        const long long total_groups = static_cast<long long>(op.rows) * (ldp / 4);
+        const int blocks = static_cast<int>(std::min<long long>((total_groups + 255) / 256, 148LL * 8));
+        if (blocks > 0) {
+            split_tf32_kernel<<<blocks, 256, 0, stream>>>(src, ld, op.rows, op.cols, hi, lo, ldp,
+                                                         (ld % 4 == 0 && aligned16(src)) ? 1 : 0);
+            MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");
+        }
+        op.base = hi;
+        op.ld = ldp;
+        op.plane_stride = cfg.planes == 2 ? static_cast<long long>(pf) : 0;
+        op.needs_prepass = true;
+    }
+
+    // --- TMA descriptors ---
+    CUtensorMap map_a, map_b;
+    {
+        const PreparedOperand& A = ops[0];
+        // K-major A: box 32 (K) x 128 (M); MN-major A: box 32 (M) x 32 (K).
+        MFB_TRY(encode_operand(&map_a, A.base, A.rows, A.cols, A.ld, cfg.planes, A.plane_stride, 32,
+                               cfg.a_mn ? 32 : kBM, cfg.a_mn != 0));
+        const PreparedOperand& B = ops[1];
+        MFB_TRY(encode_operand(&map_b, B.base, B.rows, B.cols, B.ld, cfg.planes, B.plane_stride, 32,
+                               cfg.b_mn ? 32 : cfg.bn, cfg.b_mn != 0));
+    }
+
+    GemmTcParams p{};
+    p.m = d.m;
+    p.n = d.n;
+    p.k = d.k;
+    p.num_kb = (d.k + kBK - 1) / kBK;
+    p.tiles_m = (d.m + kBM - 1) / kBM;
+    p.tiles_n = (d.n + cfg.bn - 1) / cfg.bn;
+    p.group_m = 16;
+    p.c = c;
+    p.ldc = d.ldc;
+    p.alpha = d.alpha;
+    p.beta = d.beta;
+    p.bias = bias;
+    p.epilogue = d.epilogue;
+    p.c_vec4 = (aligned16(c) && d.ldc % 4 == 0) ? 1 : 0;
+    p.wait_limit_ns = wait_limit_ns();
+
+    const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+    if (tiles > 0x7fffffffLL) return fail(MFB_EINVAL, "problem has too many output tiles");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const long long grid = std::min<long long>(tiles, sm_count(dev));  // persistent: one CTA per SM
+    static std::mutex attr_mutex;
+    {
+        std::lock_guard<std::mutex> lock(attr_mutex);
+        MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem),
+                     "cudaFuncSetAttribute(max dynamic smem)");
+    }
+    void* args[] = {&map_a, &map_b, &p};
+    MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(192), args,
+                                  static_cast<size_t>(e->smem), stream),
+                 "tcgen05 GEMM launch");
+    return MFB_OK;
+}
+
+}  // namespace mfb

@@ -1,0 +1,6 @@
+// Single translation unit of libmfb.so: the device status word (mfb::g_status) is
+// defined once and named directly by every kernel without relocatable device code.
+#include "mfb_abi.cu"
+#include "gemm_tc.cu"
+#include "gemv.cu"
+#include "conv.cu"

@@ -1,0 +1,106 @@
+// Host-side internals shared by the translation units of libmfb.so.
+#pragma once
+
+#include "../../include/mfb.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+namespace mfb {
+
+// Records `msg` as the calling thread's mfb_last_error() text and returns `status`.
+mfb_status_t fail(mfb_status_t status, const std::string& msg);
+mfb_status_t cuda_fail(cudaError_t err, const char* what);
+void clear_error();
+
+#define MFB_CUDA_TRY(expr, what)                                    \
+    do {                                                            \
+        cudaError_t mfb_err_ = (expr);                              \
+        if (mfb_err_ != cudaSuccess) return ::mfb::cuda_fail(mfb_err_, what); \
+    } while (0)
+
+#define MFB_TRY(expr)                          \
+    do {                                       \
+        mfb_status_t mfb_st_ = (expr);         \
+        if (mfb_st_ != MFB_OK) return mfb_st_; \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+class DeviceGuard {
+public:
+    DeviceGuard() { cudaGetDevice(&saved_); }
+    ~DeviceGuard() { cudaSetDevice(saved_); }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int saved_ = 0;
+};
+
+// Makes `device` current after checking it exists and is an sm_100 part.
+mfb_status_t select_device(int device);
+int sm_count(int device);
+uint64_t wait_limit_ns();
+bool stream_capturing(cudaStream_t stream);
+
+// Scratch memory: per-(device, stream) grow-only buffers for calls without a plan.
+mfb_status_t stream_workspace(int device, cudaStream_t stream, size_t bytes, void** out);
+
+// Validates a GEMM description (shapes, strides, options) against the reference's rules.
+mfb_status_t validate_desc(const mfb_gemm_desc* d, const float* a, const float* b, const float* c,
+                           const float* bias, bool need_bias_check);
+
+// ---------------------------------------------------------------------- tcgen05 GEMM
+struct TcConfig {
+    int bn = 128;
+    int stages = 3;
+    int planes = 2;   // 2 = strict 3xTF32, 1 = TF32
+    int a_mn = 0;     // A stored transposed (MN-major)
+    int b_mn = 1;     // B stored untransposed (MN-major)
+};
+
+// Admissible tile configurations for a problem, best-guess first.
+int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out);
+
+struct OperandLayout {
+    int rows = 0, cols = 0;     // stored matrix
+    long long ld = 0;           // elements
+    size_t plane_floats = 0;    // floats per split plane (0 when used in place)
+};
+
+// Scratch the tcgen05 path needs for `d` (split planes or repacked operands).
+size_t tc_workspace_bytes(const mfb_gemm_desc& d, const float* a, const float* b, bool assume_aligned_inputs);
+
+// Runs the tcgen05 GEMM (with its split/pack prepass) on `stream`.
+mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
+                     const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes);
+
+// C = beta * C, then the epilogue; the k == 0 / alpha == 0 path.
+mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c, const float* bias);
+
+// ---------------------------------------------------------------------- GEMV
+bool gemv_eligible(const mfb_gemm_desc& d);
+size_t gemv_workspace_bytes(const mfb_gemm_desc& d);
+mfb_status_t gemv_launch(const mfb_gemm_desc& d, cudaStream_t stream, const float* a, const float* b, float* c,
+                         const float* bias, void* workspace, size_t workspace_bytes);
+
+// ---------------------------------------------------------------------- conv
+mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
+                           int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
+                           int precision);
+
+// ---------------------------------------------------------------------- naive
+mfb_status_t naive_launch(const mfb_gemm_desc& d, cudaStream_t stream, const float* a, const float* b, float* c,
+                          const float* bias);
+
+// ---------------------------------------------------------------------- probes
+mfb_status_t probe_wait_launch(cudaStream_t stream, uint64_t limit_ns);
+mfb_status_t read_and_clear_status(uint32_t* bits);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace mfb
