@@ -1,0 +1,392 @@
+#!/usr/bin/env python
+"""bench.py — throughput of the dense FP32 contraction hot path on B200.
+
+Workload (default, `--workload linear`): the linear-layer GEMM configuration
+m=8192 (per GPU), k=4096, n=11008, lda=4128, ldb=ldc=11040, A ~ N(0,1),
+B ~ N(0, 1/64) (std 1/sqrt(4096)), C ~ N(0,1), alpha=0.5, beta=1, strict FP32
+(3xTF32 on tcgen05). One step = one pass of the hot path over one batch:
+split prepass + tcgen05 GEMM; with N > 1 GPUs each rank owns 8192 rows of A and C
+(weak scaling) and B is broadcast from rank 0 over NVLink by NCCL inside the step,
+in K panels overlapped with the per-panel GEMM.
+
+Prints ONE JSON line (rank 0). `--impl reference` times the reference's own CPU
+gemm_f32 (oracle/_ref, built from the reference sources) on the same configuration.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mfb|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FP32 GEMM TFLOPS (N=2048/8192) at 1/2/4/8 B200, % of roofline; GEMV GB/s"
+
+WORKLOADS = {
+    # name: (m per GPU, n, k, lda, ldb, ldc, alpha, beta, description); A, C ~ N(0,1), B ~ N(0, 1/64)
+    "linear": (8192, 11008, 4096, 4096 + 32, 11008 + 32, 11008 + 32, 0.5, 1.0,
+               "linear-layer GEMM m=8192/GPU k=4096 n=11008, lda=4128 ldb=ldc=11040, alpha=0.5 beta=1"),
+    "linear_m2048": (2048, 11008, 4096, 4096 + 32, 11008 + 32, 11008 + 32, 0.5, 1.0,
+                     "linear-layer GEMM with m=2048/GPU (profiling size; B alone exceeds L2)"),
+    "square8192": (8192, 8192, 8192, 8192, 8192, 8192, 1.0, 0.0, "square GEMM 8192^3, alpha=1 beta=0"),
+    "square2048": (2048, 2048, 2048, 2048, 2048, 2048, 1.0, 0.0, "square GEMM 2048^3, alpha=1 beta=0"),
+    "c5": (32768, 32768, 32768, 32768, 32768, 32768, 1.0, 0.0,
+           "square GEMM 32768^3 rows split across GPUs (32768 rows total), B broadcast"),
+}
+
+
+def read_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def read_profile_traffic(kernel_tag: str):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/ (a 'traffic_bytes_per_launch' line)."""
+    path = os.path.join(ROOT, "profiles", f"{kernel_tag}.md")
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", text)
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """Samples SM clock, power and throttle reasons through NVML (read-only) every 10 ms
+    while the timed region runs, on a background thread."""
+
+    # nvmlClocksEventReason bits (nvml.h): the ones a run must report.
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []
+        self.error = None
+        self._stop = None
+        self._thread = None
+
+    def _handle(self, nv):
+        # Match the CUDA device to its NVML handle by PCI bus id (CUDA_VISIBLE_DEVICES may renumber).
+        import torch
+        props = torch.cuda.get_device_properties(self.cuda_index)
+        want = getattr(props, "pci_bus_id", None)
+        for i in range(nv.nvmlDeviceGetCount()):
+            h = nv.nvmlDeviceGetHandleByIndex(i)
+            if want is None:
+                return h
+            pci = nv.nvmlDeviceGetPciInfo(h)
+            if (pci.bus, pci.device, pci.domain) == (want, getattr(props, "pci_device_id", pci.device),
+                                                     getattr(props, "pci_domain_id", pci.domain)):
+                return h
+        return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
+
+    def __enter__(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception as exc:  # sampling is reported, never required
+            self.error = f"nvml unavailable: {exc}"
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((float(sm), pw, int(rs)))
+                except Exception as exc:
+                    self.error = str(exc)
+                    return
+                self._stop.wait(0.01)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": getattr(self, "max_mhz", None),
+                    "reasons": [self.error or "no samples"], "samples": 0}
+        reasons = sorted({name for (_, _, r) in self.samples for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(s for s, _, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples),
+                "power_w_max": max(p for _, p, _ in self.samples), "source": "NVML, 10 ms period"}
+
+
+def cpu_reference_sample(m, n, k, lda, ldb, ldc, alpha, beta, rows, reps, warm=1, seed=20261001):
+    """Times the reference's compiled gemm_f32 on `rows` rows of the workload; returns TFLOPS."""
+    import oracle
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((rows, lda), dtype=np.float32)
+    b = (rng.standard_normal((k, ldb), dtype=np.float32) / 64.0).astype(np.float32)
+    c = rng.standard_normal((rows, ldc), dtype=np.float32)
+    impl = "reference" if oracle.reference_available() else "restatement"
+    times = []
+    for i in range(warm + reps):
+        cc = c.copy()
+        t0 = time.perf_counter()
+        oracle.gemm_f32(rows, n, k, a, lda, b, ldb, cc, ldc, alpha, beta, impl=impl)
+        dt = time.perf_counter() - t0
+        if i >= warm:
+            times.append(dt)
+    flops = 2.0 * rows * n * k
+    info = oracle.reference_info() if impl == "reference" else {"worker_count": 1, "gemm_kernel_name": "port"}
+    med = statistics.median(times)
+    return {
+        "tflops": flops / med / 1e12,
+        "cores": int(info["worker_count"]),
+        "kind": "reference" if impl == "reference" else "port",
+        "kernel": info["gemm_kernel_name"],
+        "seconds_per_rep": med,
+        "rows": rows,
+    }
+
+
+def run_reference_arm(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    m, n, k, lda, ldb, ldc, alpha, beta, desc = wl
+    rows = min(m, args.ref_rows)
+    import oracle
+    if not oracle.reference_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libmfref_cpu.so was not built "
+                          "(build() compiles it where the reference sources exist)"}))
+        return 0
+    steps = []
+    rng = np.random.default_rng(20261001)
+    a = rng.standard_normal((rows, lda), dtype=np.float32)
+    b = (rng.standard_normal((k, ldb), dtype=np.float32) / 64.0).astype(np.float32)
+    c = rng.standard_normal((rows, ldc), dtype=np.float32)
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        oracle.gemm_f32(rows, n, k, a, lda, b, ldb, c, ldc, alpha, beta, impl="reference")
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            steps.append(dt)
+    total = sum(steps)
+    tflops = 2.0 * rows * n * k * len(steps) / total / 1e12
+    info = oracle.reference_info()
+    sample = (f"{rows} of the {m} rows per step (full n={n}, k={k}); reference gemm_f32 "
+              f"({info['gemm_kernel_name']}) compiled from the reference sources; pool of {info['worker_count']} "
+              f"threads, rows split into ~8 chunks by the reference (grain m/8)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tflops, "unit": "TFLOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": desc, "rows_per_step_sample": rows, "precision": "fp32 (CPU FMA)"},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOPS", "cores": info["worker_count"], "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": tflops, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["mfb", "reference"], default="mfb")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="linear")
+    ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-rows", type=int, default=2048, help="rows per reference-arm step (bounded sample)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference_arm(args, wl)
+
+    import torch
+    import torch.distributed as dist
+    import matrixflash_pro_b200 as mf
+    from matrixflash_pro_b200.distributed import RowSplitGemm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    m_total, n, k, lda, ldb, ldc, alpha, beta, desc = wl
+    if args.workload == "c5":
+        m = -(-m_total // world)  # strong scaling: the rows of one product split across ranks
+        scaling = "strong"
+    else:
+        m = m_total               # weak scaling: m rows per GPU
+        scaling = "weak"
+    precision = mf.GemmPrecision.fp32 if args.precision == "fp32" else mf.GemmPrecision.tf32
+
+    gen = torch.Generator(device="cuda").manual_seed(20261001 + rank)
+    A_buf = torch.randn((m, lda), device="cuda", generator=gen)
+    B_buf = torch.randn((k, ldb), device="cuda", generator=torch.Generator(device="cuda").manual_seed(7)) / 64.0
+    C_buf = torch.randn((m, ldc), device="cuda", generator=gen)
+    A, B, C = A_buf[:, :k], B_buf[:, :n], C_buf[:, :n]
+    op = RowSplitGemm(m, n, k, lda, ldb, ldc, precision)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        op(A, B, C, alpha, beta)
+    torch.cuda.synchronize()
+    mf.sync()
+
+    # ---------------------------------------------------------------- timed region (device)
+    stream = torch.cuda.current_stream()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kernel_ms = 0.0
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        e_start.record(stream)
+        kernel_records = []
+        for _ in range(args.steps):
+            op(A, B, C, alpha, beta, time_kernels=True)
+            kernel_records.extend(op.kernel_events)
+        e_end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    elapsed_ms = e_start.elapsed_time(e_end)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in kernel_records)
+    mf.sync()  # raises on a device-side timeout
+
+    t = torch.tensor([elapsed_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    flops_per_rank_step = 2.0 * m * n * k
+    value = world * flops_per_rank_step * args.steps / (max_ms / 1e3) / 1e12
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    e2e = None
+    if args.e2e_steps > 0:
+        A_h = torch.empty((m, lda), dtype=torch.float32, pin_memory=True)
+        B_h = torch.empty((k, ldb), dtype=torch.float32, pin_memory=True)
+        C_h = torch.empty((m, ldc), dtype=torch.float32, pin_memory=True)
+        A_h.copy_(A_buf)
+        B_h.copy_(B_buf)
+        C_h.copy_(C_buf)
+        C_out = torch.empty_like(C_h).pin_memory()
+        h2d = A_h.numel() * 4 + C_h.numel() * 4 + (B_h.numel() * 4 if rank == 0 else 0)
+        d2h = C_out.numel() * 4
+
+        def e2e_step():
+            A_buf.copy_(A_h, non_blocking=True)
+            if rank == 0:
+                B_buf.copy_(B_h, non_blocking=True)
+            C_buf.copy_(C_h, non_blocking=True)
+            op(A, B, C, alpha, beta)
+            C_out.copy_(C_buf, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t2 = torch.tensor([s0.elapsed_time(s1)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t2.item())
+        e2e = {"value": world * flops_per_rank_step * args.e2e_steps / (e2e_ms / 1e3) / 1e12, "unit": "TFLOPS",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps,
+               "path": "pinned host A/B/C -> device, RowSplitGemm (C ABI plans), device C -> pinned host"}
+
+    # ---------------------------------------------------------------- roofline of the GEMM kernel
+    peaks, peak_src = read_peaks()
+    strict = precision == mf.GemmPrecision.fp32
+    passes = 6.0 if strict else 2.0   # TF32 runs at half the bf16 rate; strict = 3 TF32 passes
+    peak_sust = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) / passes
+    gemm_flops = flops_per_rank_step * args.steps
+    achieved = gemm_flops / (kernel_ms / 1e3) / 1e12 if kernel_ms > 0 else None
+    launches_gemm = len(op.plans) * args.steps
+    tag = f"gemm_{'3xtf32' if strict else 'tf32'}_{args.workload}"
+    traffic = read_profile_traffic(tag)
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
+                "frac": (achieved / peak_sust) if achieved else None, "traffic": traffic,
+                "kernel": "gemm_tf32_tc_kernel (tcgen05 kind::tf32, " + ("3xTF32" if strict else "1xTF32") + ")",
+                "peak_basis": f"{'bf16_tflops_sustained/6' if strict else 'bf16_tflops_sustained/2'} "
+                              f"({peak_src} MEASURED_PEAKS.json; TF32 = bf16/2, strict = 3 TF32 passes)",
+                "peak_burst": peaks["bf16_tflops"] / passes,
+                "kernel_ms_per_launch": kernel_ms / max(1, launches_gemm),
+                "flops_per_launch": gemm_flops / max(1, launches_gemm)}
+
+    # ---------------------------------------------------------------- CPU baseline (rank 0, N=1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            rows = 1024 if args.workload in ("linear", "square8192") else min(256, m)
+            r = cpu_reference_sample(m, n, k, lda, ldb, ldc, alpha, beta, rows, reps=3)
+            cpu = {"value": r["tflops"], "unit": "TFLOPS", "cores": r["cores"], "kind": r["kind"],
+                   "sample": f"{rows} rows x n={n} x k={k} of the same workload, 1 warm-up + median of 3 "
+                             f"({r['seconds_per_rep']:.2f} s each), gemm_f32 kernel {r['kernel']}, "
+                             f"nproc={os.cpu_count()}"}
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "TFLOPS", "cores": None, "kind": None, "sample": f"failed: {exc}"}
+
+    clk = clocks.summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": desc, "m_per_gpu": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "ldc": ldc,
+                       "precision": "strict fp32 (3xTF32 tcgen05)" if strict else "tf32 (tcgen05)",
+                       "parallelism": f"row-split x{world}" + (", B broadcast by NCCL in K panels" if world > 1
+                                                               else ""),
+                       "l2": "inputs larger than L2 (126 MB) every step",
+                       "global_batch": m * world, "seq_len": None},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": op.launches_per_step() * args.steps, "clocks": clk,
+        }
+        print(json.dumps(line))
+    op.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -134,6 +134,17 @@ typedef struct mfb_plan_info {
 MFB_API mfb_status_t mfb_plan_create(int device, const mfb_gemm_desc* desc, mfb_plan_t* out);
 MFB_API mfb_status_t mfb_plan_execute(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
                                       float* c, float alpha, float beta, const float* bias);
+/* The two phases of mfb_plan_execute, for callers that reuse prepared operands or
+ * time the phases: prepare runs the operand prepass (3xTF32 hi/lo split, or repacking
+ * of operands TMA cannot address in place) into the plan's scratch; multiply runs only
+ * the GEMM kernel on them (a/b are still read when used in place). No reference
+ * counterpart: GemmPlan::execute (gemm.hpp:47) is both phases in one call. */
+MFB_API mfb_status_t mfb_plan_prepare(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b);
+MFB_API mfb_status_t mfb_plan_multiply(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
+                                       float* c, float alpha, float beta, const float* bias);
+/* Caps the persistent GEMM grid at `sms` SMs (0 = all), leaving the rest to work that
+ * must run concurrently, e.g. an NCCL broadcast of the next K panel. */
+MFB_API mfb_status_t mfb_plan_set_sm_limit(mfb_plan_t plan, int sms);
 /* Times every admissible tile configuration on `scratch_c` (an m x n buffer with ldc
  * of the plan; c is never touched), keeps the fastest, and reports it. Synchronizes. */
 MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,

@@ -7,7 +7,7 @@ Drop-in for MatrixFlash-Pro's GEMM / GEMV / conv2d-forward hot path:
 """
 from .errors import (CudaError, DeviceTimeoutError, InvalidArgumentError, MatrixProError,  # noqa: F401
                      ShapeMismatchError)
-from .gemm import (GemmEpilogue, GemmOptions, GemmPlan, GemmPrecision, GemmTuningResult, cuda_gemm,  # noqa: F401
+from .gemm import (GemmEpilogue, GemmOptions, GemmPlan, GemmPrecision, GemmTuningResult, checked_dim, cuda_gemm,  # noqa: F401,E501
                    cuda_sync, device_status, gemm, gemm_bias_gelu, gemm_bias_relu, gemm_into, gemv,
                    get_wait_limit_ns, make_desc, multiply, multiply_into, naive_sgemm, set_wait_limit_ns, sgemm,
                    sgemm_ptr, sync)

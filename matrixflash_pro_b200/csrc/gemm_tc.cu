@@ -261,9 +261,12 @@ mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c,
 }
 
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
-                     const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes) {
+                     const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
+                     int phases, int sm_limit) {
     const TcEntry* e = find_kernel(cfg);
     if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 kernel for this tile configuration");
+    const bool run_prepass = (phases & kPhasePrepare) != 0;
+    const bool run_gemm = (phases & kPhaseMultiply) != 0;
 
     // --- operand preparation: split planes (strict) or repack (TF32, unaligned) ---
     PreparedOperand ops[2];
@@ -290,7 +293,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         used += need;
         const long long total_groups = static_cast<long long>(op.rows) * (ldp / 4);
         const int blocks = static_cast<int>(std::min<long long>((total_groups + 255) / 256, 148LL * 8));
-        if (blocks > 0) {
+        if (run_prepass && blocks > 0) {
             split_tf32_kernel<<<blocks, 256, 0, stream>>>(src, ld, op.rows, op.cols, hi, lo, ldp,
                                                          (ld % 4 == 0 && aligned16(src)) ? 1 : 0);
             MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");
@@ -300,6 +303,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         op.plane_stride = cfg.planes == 2 ? static_cast<long long>(pf) : 0;
         op.needs_prepass = true;
     }
+    if (!run_gemm) return MFB_OK;
 
     // --- TMA descriptors ---
     CUtensorMap map_a, map_b;
@@ -334,7 +338,9 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     if (tiles > 0x7fffffffLL) return fail(MFB_EINVAL, "problem has too many output tiles");
     int dev = 0;
     cudaGetDevice(&dev);
-    const long long grid = std::min<long long>(tiles, sm_count(dev));  // persistent: one CTA per SM
+    // Persistent: one CTA per SM, or fewer when the caller leaves SMs to a concurrent collective.
+    const int sms = sm_limit > 0 ? std::min(sm_limit, sm_count(dev)) : sm_count(dev);
+    const long long grid = std::min<long long>(tiles, sms);
     static std::mutex attr_mutex;
     {
         std::lock_guard<std::mutex> lock(attr_mutex);

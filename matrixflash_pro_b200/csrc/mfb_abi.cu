@@ -196,9 +196,58 @@ struct mfb_plan {
     TcConfig cfg{};
     TcConfig candidates[16];
     int n_candidates = 0;
+    int sm_limit = 0;
     void* ws = nullptr;
     size_t ws_bytes = 0;
 };
+
+namespace {
+
+// Shared body of mfb_plan_execute / mfb_plan_prepare / mfb_plan_multiply.
+mfb_status_t plan_run(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, const float* b, float* c,
+                      float alpha, float beta, const float* bias, int phases) {
+    clear_error();
+    if (!plan) return fail(MFB_EINVAL, "Cannot execute a null or destroyed GEMM plan");
+    mfb_gemm_desc d = plan->desc;
+    d.alpha = alpha;
+    d.beta = beta;
+    const bool multiply = (phases & kPhaseMultiply) != 0;
+    if (multiply) {
+        MFB_TRY(validate_desc(&d, a, b, c, bias, true));
+    } else if (d.m > 0 && d.n > 0 && d.k > 0 && (!a || !b)) {
+        return fail(MFB_EINVAL, "null A or B pointer");
+    }
+    DeviceGuard guard;
+    MFB_TRY(select_device(plan->device));
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_h);
+    int path = plan->path;
+    if ((path == kPathTc || path == kPathGemv) && alpha == 0.0f && multiply) path = kPathScale;
+    switch (path) {
+        case kPathEmpty: return MFB_OK;
+        case kPathScale: return multiply ? scale_output(d, stream, c, bias) : MFB_OK;
+        case kPathGemv: return multiply ? gemv_launch(d, stream, a, b, c, bias, plan->ws, plan->ws_bytes) : MFB_OK;
+        default: break;
+    }
+    const size_t need = tc_workspace_bytes(d, a, b, false);
+    if (need > plan->ws_bytes) {
+        // Only a TF32 plan given unaligned operands lands here: grow once, outside capture.
+        if (stream_capturing(stream))
+            return fail(MFB_EINVAL, "TF32 plan got operands that are not 16-byte aligned during graph capture");
+        MFB_CUDA_TRY(cudaStreamSynchronize(stream), "plan workspace resize sync");
+        if (plan->ws) cudaFree(plan->ws);
+        plan->ws = nullptr;
+        plan->ws_bytes = 0;
+        cudaError_t e = cudaMalloc(&plan->ws, need);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return cuda_fail(e, "plan workspace cudaMalloc");
+        }
+        plan->ws_bytes = need;
+    }
+    return tc_gemm(d, plan->cfg, stream, a, b, c, bias, plan->ws, plan->ws_bytes, phases, plan->sm_limit);
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -347,41 +396,24 @@ MFB_API mfb_status_t mfb_plan_create(int device, const mfb_gemm_desc* desc, mfb_
 
 MFB_API mfb_status_t mfb_plan_execute(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, const float* b,
                                       float* c, float alpha, float beta, const float* bias) {
+    return plan_run(plan, stream_h, a, b, c, alpha, beta, bias, kPhaseAll);
+}
+
+MFB_API mfb_status_t mfb_plan_prepare(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, const float* b) {
+    return plan_run(plan, stream_h, a, b, nullptr, 1.0f, 0.0f, nullptr, kPhasePrepare);
+}
+
+MFB_API mfb_status_t mfb_plan_multiply(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, const float* b,
+                                       float* c, float alpha, float beta, const float* bias) {
+    return plan_run(plan, stream_h, a, b, c, alpha, beta, bias, kPhaseMultiply);
+}
+
+MFB_API mfb_status_t mfb_plan_set_sm_limit(mfb_plan_t plan, int sms) {
     clear_error();
-    if (!plan) return fail(MFB_EINVAL, "Cannot execute a null or destroyed GEMM plan");
-    mfb_gemm_desc d = plan->desc;
-    d.alpha = alpha;
-    d.beta = beta;
-    MFB_TRY(validate_desc(&d, a, b, c, bias, true));
-    DeviceGuard guard;
-    MFB_TRY(select_device(plan->device));
-    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_h);
-    int path = plan->path;
-    if (path == kPathTc && alpha == 0.0f) path = kPathScale;
-    if (path == kPathGemv && alpha == 0.0f) path = kPathScale;
-    switch (path) {
-        case kPathEmpty: return MFB_OK;
-        case kPathScale: return scale_output(d, stream, c, bias);
-        case kPathGemv: return gemv_launch(d, stream, a, b, c, bias, plan->ws, plan->ws_bytes);
-        default: break;
-    }
-    const size_t need = tc_workspace_bytes(d, a, b, false);
-    if (need > plan->ws_bytes) {
-        // Only a TF32 plan given unaligned operands lands here: grow once, outside capture.
-        if (stream_capturing(stream))
-            return fail(MFB_EINVAL, "TF32 plan got operands that are not 16-byte aligned during graph capture");
-        MFB_CUDA_TRY(cudaStreamSynchronize(stream), "plan workspace resize sync");
-        if (plan->ws) cudaFree(plan->ws);
-        plan->ws = nullptr;
-        plan->ws_bytes = 0;
-        cudaError_t e = cudaMalloc(&plan->ws, need);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return cuda_fail(e, "plan workspace cudaMalloc");
-        }
-        plan->ws_bytes = need;
-    }
-    return tc_gemm(d, plan->cfg, stream, a, b, c, bias, plan->ws, plan->ws_bytes);
+    if (!plan) return fail(MFB_EINVAL, "null plan");
+    if (sms < 0) return fail(MFB_EINVAL, "SM limit must be >= 0 (0 = all SMs)");
+    plan->sm_limit = sms;
+    return MFB_OK;
 }
 
 MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, const float* b,

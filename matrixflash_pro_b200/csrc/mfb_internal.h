@@ -75,9 +75,14 @@ struct OperandLayout {
 // Scratch the tcgen05 path needs for `d` (split planes or repacked operands).
 size_t tc_workspace_bytes(const mfb_gemm_desc& d, const float* a, const float* b, bool assume_aligned_inputs);
 
-// Runs the tcgen05 GEMM (with its split/pack prepass) on `stream`.
+// Runs the tcgen05 GEMM on `stream`: kPhasePrepare launches the split/pack prepass of
+// the operands into `workspace`, kPhaseMultiply the GEMM kernel on the prepared
+// operands (a/b are still needed for operands used in place). sm_limit > 0 caps the
+// persistent grid.
+enum { kPhasePrepare = 1, kPhaseMultiply = 2, kPhaseAll = 3 };
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
-                     const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes);
+                     const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
+                     int phases = kPhaseAll, int sm_limit = 0);
 
 // C = beta * C, then the epilogue; the k == 0 / alpha == 0 path.
 mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c, const float* bias);

@@ -317,6 +317,27 @@ class GemmPlan:
                                                _ptr(output), float(alpha), float(beta), _ptr(bias)),
                    "GemmPlan.execute")
 
+    def prepare(self, left: torch.Tensor, right: torch.Tensor) -> None:
+        """Operand prepass only (3xTF32 split into the plan's scratch); see mfb_plan_prepare."""
+        if not self._handle:
+            raise InvalidArgumentError("Cannot execute a moved-from GEMM plan")
+        _lib.check(_lib.lib().mfb_plan_prepare(self._handle, _stream_handle(self.stream), _ptr(left), _ptr(right)),
+                   "GemmPlan.prepare")
+
+    def multiply(self, left: torch.Tensor, right: torch.Tensor, output: torch.Tensor, alpha: float = 1.0,
+                 beta: float = 0.0, bias: torch.Tensor | None = None) -> None:
+        """GEMM kernel only, on operands prepared by prepare(); see mfb_plan_multiply."""
+        if not self._handle:
+            raise InvalidArgumentError("Cannot execute a moved-from GEMM plan")
+        self._validate(left, right, output, bias)
+        _lib.check(_lib.lib().mfb_plan_multiply(self._handle, _stream_handle(self.stream), _ptr(left), _ptr(right),
+                                                _ptr(output), float(alpha), float(beta), _ptr(bias)),
+                   "GemmPlan.multiply")
+
+    def set_sm_limit(self, sms: int) -> None:
+        """Cap the persistent GEMM grid (0 = all SMs)."""
+        _lib.check(_lib.lib().mfb_plan_set_sm_limit(self._handle, int(sms)), "GemmPlan.set_sm_limit")
+
     def tune(self, left: torch.Tensor, right: torch.Tensor, output: torch.Tensor, alpha: float = 1.0,
              beta: float = 0.0, bias: torch.Tensor | None = None, repeats: int = 5) -> GemmTuningResult:
         """Times every admissible tile configuration on a scratch output (output and
