@@ -135,9 +135,9 @@ MFB_API mfb_status_t mfb_plan_create(int device, const mfb_gemm_desc* desc, mfb_
 MFB_API mfb_status_t mfb_plan_execute(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
                                       float* c, float alpha, float beta, const float* bias);
 /* The two phases of mfb_plan_execute, for callers that reuse prepared operands or
- * time the phases: prepare runs the operand prepass (3xTF32 hi/lo split, or repacking
- * of operands TMA cannot address in place) into the plan's scratch; multiply runs only
- * the GEMM kernel on them (a/b are still read when used in place). No reference
+ * time the phases: prepare runs the operand prepass (3xTF32 hi/lo split, or TF32
+ * round-to-nearest) into the plan's scratch; multiply runs only the GEMM kernel on the
+ * prepared operands (a/b are still passed; GEMV plans read them there). No reference
  * counterpart: GemmPlan::execute (gemm.hpp:47) is both phases in one call. */
 MFB_API mfb_status_t mfb_plan_prepare(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b);
 MFB_API mfb_status_t mfb_plan_multiply(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,

@@ -1,5 +1,5 @@
-// Host side of the tcgen05 GEMM: operand preparation (3xTF32 split planes or
-// repacking of operands TMA cannot address in place), TMA descriptor encoding,
+// Host side of the tcgen05 GEMM: operand preparation (3xTF32 hi/lo split planes, or
+// one round-to-nearest TF32 plane per operand), TMA descriptor encoding,
 // tile-configuration choice and launch. The reference's cuBLAS/cuBLASLt bodies
 // this replaces: src/hw/cuda_backend.cu:91-99 and
 // src/ops/gemm/plan/implementation.inc:111-151.
@@ -23,8 +23,9 @@ __device__ __forceinline__ float round_tf32(float x) {
 }
 
 // hi = tf32(x) (round to nearest), lo = tf32(x - hi); x - hi is exact in FP32, so
-// hi + lo carries 22 significant bits of x. lo == nullptr copies x unchanged into hi
-// (repacking to a TMA-addressable layout, used by the TF32 mode).
+// hi + lo carries 22 significant bits of x. lo == nullptr writes only hi: the TF32
+// mode's operands, rounded to nearest like cuBLAS/CUTLASS TF32 conversion (the tensor
+// core itself would truncate the low 13 bits, a bias that shows on same-sign data).
 __global__ void split_tf32_kernel(const float* __restrict__ x, long long ldx, int rows, int cols,
                                   float* __restrict__ hi, float* __restrict__ lo, long long ldp, int vec_in) {
     const long long groups_per_row = ldp / 4;
@@ -54,7 +55,7 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, long long ldx, in
             l = make_float4(lv[0], lv[1], lv[2], lv[3]);
             *reinterpret_cast<float4*>(lo + r * ldp + c0) = l;
         } else {
-            h = make_float4(v[0], v[1], v[2], v[3]);
+            h = make_float4(round_tf32(v[0]), round_tf32(v[1]), round_tf32(v[2]), round_tf32(v[3]));
         }
         *reinterpret_cast<float4*>(hi + r * ldp + c0) = h;
     }
@@ -130,19 +131,23 @@ struct TcEntry {
     int bn, stages, planes, a_mn, b_mn;
     const void* fn;
     int smem;
+    int threads;
 };
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
 TcEntry make_entry() {
+    using L = GemmTcSmem<BN, STAGES, PLANES>;
     return TcEntry{BN, STAGES, PLANES, A_MN, B_MN,
-                   reinterpret_cast<const void*>(&gemm_tf32_tc_kernel<BN, STAGES, PLANES, A_MN, B_MN>),
-                   GemmTcSmem<BN, STAGES, PLANES>::kBytes};
+                   reinterpret_cast<const void*>(&gemm_tf32_tc_kernel<BN, STAGES, PLANES, A_MN, B_MN>), L::kBytes,
+                   L::kThreads};
 }
 
 const TcEntry* kernel_table(int* count) {
     static const TcEntry table[] = {
         // strict FP32 (3xTF32 split planes, chunked round-to-nearest accumulation)
+        make_entry<256, 2, 2, 0, 1>(),
         make_entry<128, 3, 2, 0, 1>(),
+        make_entry<64, 4, 2, 0, 1>(),
         make_entry<128, 3, 2, 1, 1>(),
         make_entry<128, 3, 2, 0, 0>(),
         make_entry<128, 3, 2, 1, 0>(),
@@ -234,19 +239,15 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
     return n_out;
 }
 
-size_t tc_workspace_bytes(const mfb_gemm_desc& d, const float* a, const float* b, bool assume_aligned_inputs) {
+size_t tc_workspace_bytes(const mfb_gemm_desc& d) {
     size_t bytes = 0;
     for (int which = 0; which < 2; ++which) {
         int rows, cols;
         long long ld;
         stored_dims(d, which == 0, &rows, &cols, &ld);
-        const float* p = which == 0 ? a : b;
-        if (d.precision == MFB_PRECISION_TF32) {
-            const bool in_place = (ld % 4 == 0) && (assume_aligned_inputs || aligned16(p));
-            if (!in_place) bytes += plane_floats(rows, cols) * 4;
-        } else {
-            bytes += 2 * plane_floats(rows, cols) * 4;
-        }
+        (void)ld;
+        // TF32: one round-to-nearest plane per operand; strict: hi and lo planes.
+        bytes += (d.precision == MFB_PRECISION_TF32 ? 1 : 2) * plane_floats(rows, cols) * 4;
     }
     return bytes;
 }
@@ -277,12 +278,6 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         long long ld;
         stored_dims(d, which == 0, &op.rows, &op.cols, &ld);
         const float* src = which == 0 ? a : b;
-        const bool in_place = cfg.planes == 1 && (ld % 4 == 0) && aligned16(src);
-        if (in_place) {
-            op.base = src;
-            op.ld = ld;
-            continue;
-        }
         const long long ldp = round_up(op.cols, 4);
         const size_t pf = plane_floats(op.rows, op.cols);
         const size_t need = pf * 4 * static_cast<size_t>(cfg.planes);
@@ -348,7 +343,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
                      "cudaFuncSetAttribute(max dynamic smem)");
     }
     void* args[] = {&map_a, &map_b, &p};
-    MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(192), args,
+    MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(e->threads), args,
                                   static_cast<size_t>(e->smem), stream),
                  "tcgen05 GEMM launch");
     return MFB_OK;

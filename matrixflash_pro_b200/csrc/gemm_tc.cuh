@@ -4,25 +4,24 @@
 //   warp 0      TMA producer: one elected lane streams 32-deep K slabs of A and B
 //               into a STAGES-deep ring of swizzled shared-memory tiles, running
 //               ahead across tile boundaries.
-//   warp 1      allocates all 512 TMEM columns; one elected lane issues
+//   warp 1      allocates 2 x BN TMEM columns; one elected lane issues
 //               tcgen05.mma kind::tf32 and releases each stage with tcgen05.commit.
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns per warp, fused
+//   warps 2..   epilogue: tcgen05.ld of the FP32 accumulator, fused
 //               alpha/beta/bias/activation, strided stores to C.
 //
 // PLANES = 1 (GemmPrecision::tf32): one TF32 pass per K step into a 128 x BN FP32
 // accumulator; two accumulators alternate between tiles so the epilogue of tile i
-// overlaps the MMAs of tile i+1.
+// overlaps the MMAs of tile i+1 (4 epilogue warps, one per TMEM sub-partition).
 //
 // PLANES = 2 (strict FP32): each operand arrives as a (hi, lo) pair of TF32 planes
-// written by split_tf32_kernel (x = hi + lo + O(2^-22 |x|)). The tensor core sums
-// each MMA into its FP32 accumulator with a truncating (round-toward-zero) add, so a
-// single accumulator drifts by ~K/8 ulps. Instead:
-//   * hi*hi products go to a "big" TMEM accumulator that is restarted every
-//     kChunkKb K blocks (64 of K); the epilogue warps fold each finished chunk into
-//     FP32 registers with round-to-nearest adds (two chunk buffers alternate);
-//   * lo*hi and hi*lo go to a "small" accumulator that lives for the whole tile
-//     (its truncation error is 2^-11 smaller); the epilogue adds it at the end.
-// TMEM: big[2] x 128 columns + small[2] x 128 columns = 512 (BN = 128).
+// written by split_tf32_kernel (x = hi + lo + O(2^-22 |x|)); every K step issues
+// lo*hi, hi*lo, then hi*hi. The tensor core folds each MMA into its FP32 accumulator
+// with a truncating (round-toward-zero) add, so one accumulator over all of K drifts
+// by ~K/8 ulps (1.4e-5 normwise at K=2048, measured). The accumulator is therefore
+// restarted every kChunkKb K blocks (64 of K) and the epilogue warps fold each
+// finished chunk into FP32 registers with round-to-nearest adds; two chunk buffers
+// alternate so the MMAs never wait for the fold. 8 epilogue warps: two per TMEM
+// sub-partition, each owning BN/2 columns of its 32 rows in registers.
 //
 // Operand majors: A is K-major (row-major A) or MN-major (A stored transposed);
 // B is MN-major (row-major B) or K-major (B stored transposed). K-major tiles are one
@@ -58,7 +57,7 @@ struct GemmTcParams {
 
 constexpr int kBM = 128;
 constexpr int kBK = 32;        // 32 fp32 = 128 bytes: one swizzle row
-constexpr int kChunkKb = 2;    // strict mode: big accumulator restarts every 2 K blocks (64 of K)
+constexpr int kChunkKb = 2;    // strict mode: accumulator restarts every 2 K blocks (64 of K)
 
 template <int BN, int STAGES, int PLANES>
 struct GemmTcSmem {
@@ -67,7 +66,9 @@ struct GemmTcSmem {
     static constexpr int kStageBytes = kATileBytes + kBTileBytes;
     static constexpr int kBarrierOffset = STAGES * kStageBytes;
     static constexpr int kBytes = kBarrierOffset + 256 + 1024;  // barriers + 1 KiB alignment slack
-    static constexpr int kTmemCols = PLANES == 2 ? 512 : 2 * BN;
+    static constexpr int kTmemCols = 2 * BN;                    // two accumulator buffers
+    static constexpr int kEpiWarps = PLANES == 2 ? 8 : 4;
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };
 
 __device__ __forceinline__ float apply_epilogue_op(float v, const float* bias, int col, int epilogue) {
@@ -106,29 +107,34 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t addr, int pl, int ks) 
 }
 
 // Writes 32 consecutive outputs of one row: o = epilogue(alpha * acc + beta * C).
-__device__ __forceinline__ void store_row_chunk(float* crow, int col0, const float (&v)[32], const GemmTcParams& p) {
+__device__ __forceinline__ void store_row_chunk(float* crow, int col0, const float* v, const GemmTcParams& p) {
     if (p.c_vec4 && col0 + 32 <= p.n) {
-        float4 cin[8];
-        if (p.beta != 0.0f) {
+        // Two halves of 16: the C loads of a half are issued together, then combined and stored.
 #pragma unroll
-            for (int j = 0; j < 8; ++j) cin[j] = *reinterpret_cast<const float4*>(crow + col0 + 4 * j);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) o[e] = p.alpha * v[4 * j + e];
+        for (int h = 0; h < 2; ++h) {
+            float4 cin[4];
             if (p.beta != 0.0f) {
-                o[0] = fmaf(p.beta, cin[j].x, o[0]);
-                o[1] = fmaf(p.beta, cin[j].y, o[1]);
-                o[2] = fmaf(p.beta, cin[j].z, o[2]);
-                o[3] = fmaf(p.beta, cin[j].w, o[3]);
-            }
-            if (p.epilogue) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) o[e] = apply_epilogue_op(o[e], p.bias, col0 + 4 * j + e, p.epilogue);
+                for (int j = 0; j < 4; ++j) cin[j] = *reinterpret_cast<const float4*>(crow + col0 + 16 * h + 4 * j);
             }
-            *reinterpret_cast<float4*>(crow + col0 + 4 * j) = make_float4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int c = 16 * h + 4 * j;
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = p.alpha * v[c + e];
+                if (p.beta != 0.0f) {
+                    o[0] = fmaf(p.beta, cin[j].x, o[0]);
+                    o[1] = fmaf(p.beta, cin[j].y, o[1]);
+                    o[2] = fmaf(p.beta, cin[j].z, o[2]);
+                    o[3] = fmaf(p.beta, cin[j].w, o[3]);
+                }
+                if (p.epilogue) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) o[e] = apply_epilogue_op(o[e], p.bias, col0 + c + e, p.epilogue);
+                }
+                *reinterpret_cast<float4*>(crow + col0 + c) = make_float4(o[0], o[1], o[2], o[3]);
+            }
         }
     } else {
 #pragma unroll
@@ -144,21 +150,18 @@ __device__ __forceinline__ void store_row_chunk(float* crow, int col0, const flo
 }
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmTcSmem<BN, STAGES, PLANES>::kThreads, 1)
     gemm_tf32_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const GemmTcParams p) {
     using L = GemmTcSmem<BN, STAGES, PLANES>;
-    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
-    static_assert(PLANES == 1 || BN == 128, "strict mode uses 128 x 128 tiles (TMEM budget)");
+    static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
     uint64_t* empty_bar = full_bar + STAGES;
-    uint64_t* acc_full_bar = empty_bar + STAGES;    // [2] tile (tf32) or big-chunk (strict) buffers
-    uint64_t* acc_empty_bar = acc_full_bar + 2;     // [2]
-    uint64_t* small_full_bar = acc_empty_bar + 2;   // [2] strict only: per-tile small-term buffers
-    uint64_t* small_empty_bar = small_full_bar + 2; // [2]
-    uint64_t* drain_bar = small_empty_bar + 2;
+    uint64_t* acc_full_bar = empty_bar + STAGES;  // [2] tile (tf32) or K-chunk (strict) buffers
+    uint64_t* acc_empty_bar = acc_full_bar + 2;   // [2]
+    uint64_t* drain_bar = acc_empty_bar + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -173,9 +176,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full_bar[b], 1);
-            mbar_init(&acc_empty_bar[b], 4);  // one arrival per epilogue warp
-            mbar_init(&small_full_bar[b], 1);
-            mbar_init(&small_empty_bar[b], 4);
+            mbar_init(&acc_empty_bar[b], L::kEpiWarps);  // one arrival per epilogue warp
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -240,34 +241,25 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
         constexpr uint32_t idesc = umma_idesc_tf32(kBM, BN, A_MN, B_MN);
-        int it = 0;     // K blocks consumed (stage ring position)
-        int chunk = 0;  // strict: big-accumulator chunks issued
-        int local = 0;  // tiles of this CTA
+        // Accumulator buffers are handed out per tile (tf32) or per K chunk (strict).
+        const int kb_per_buf = PLANES == 2 ? kChunkKb : 0x7fffffff;
+        int it = 0;    // K blocks consumed (stage ring position)
+        int buf = 0;   // accumulator buffers used so far
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-            const int tb = local & 1;
-            // tf32: the tile's accumulator buffer; strict: the tile's small-term buffer.
-            uint64_t* tile_empty = PLANES == 2 ? &small_empty_bar[tb] : &acc_empty_bar[tb];
-            if (!mbar_wait_bounded(tile_empty, ((local >> 1) & 1) ^ 1, limit, abort_flag)) {
-                report_status(kStatusTimeoutMma, abort_flag);
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t tile_tmem = PLANES == 2 ? tmem_base + 256 + tb * 128 : tmem_base + tb * BN;
-            uint32_t big_tmem = 0;
-            uint32_t acc_big = 0, acc_small = 0;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            uint32_t d_tmem = 0;
+            uint32_t acc = 0;
             for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-                if (PLANES == 2 && kb % kChunkKb == 0) {
-                    const int cb = chunk & 1;
-                    if (!mbar_wait_bounded(&acc_empty_bar[cb], ((chunk >> 1) & 1) ^ 1, limit, abort_flag)) {
+                if (kb % kb_per_buf == 0) {
+                    const int b = buf & 1;
+                    if (!mbar_wait_bounded(&acc_empty_bar[b], ((buf >> 1) & 1) ^ 1, limit, abort_flag)) {
                         report_status(kStatusTimeoutMma, abort_flag);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    big_tmem = tmem_base + cb * 128;
-                    acc_big = 0;
+                    d_tmem = tmem_base + b * BN;
+                    acc = 0;
                 }
                 const int s = it % STAGES;
                 if (!mbar_wait_bounded(&full_bar[s], (it / STAGES) & 1, limit, abort_flag)) {
@@ -285,24 +277,19 @@ __global__ void __launch_bounds__(192, 1)
                     if (PLANES == 2) {
                         const uint64_t a_lo = operand_desc<A_MN, kBM, PLANES>(a_addr, 1, ks);
                         const uint64_t b_lo = operand_desc<B_MN, BN, PLANES>(b_addr, 1, ks);
-                        umma_tf32(tile_tmem, a_lo, b_hi, idesc, acc_small);
-                        acc_small = 1;
-                        umma_tf32(tile_tmem, a_hi, b_lo, idesc, 1);
-                        umma_tf32(big_tmem, a_hi, b_hi, idesc, acc_big);
-                        acc_big = 1;
-                    } else {
-                        umma_tf32(tile_tmem, a_hi, b_hi, idesc, acc_big);
-                        acc_big = 1;
+                        umma_tf32(d_tmem, a_lo, b_hi, idesc, acc);
+                        acc = 1;
+                        umma_tf32(d_tmem, a_hi, b_lo, idesc, 1);
                     }
+                    umma_tf32(d_tmem, a_hi, b_hi, idesc, acc);
+                    acc = 1;
                 }
                 umma_commit(&empty_bar[s]);
-                if (PLANES == 2 && (kb % kChunkKb == kChunkKb - 1 || kb == p.num_kb - 1)) {
-                    umma_commit(&acc_full_bar[chunk & 1]);
-                    ++chunk;
+                if (kb % kb_per_buf == kb_per_buf - 1 || kb == p.num_kb - 1) {
+                    umma_commit(&acc_full_bar[buf & 1]);
+                    ++buf;
                 }
             }
-            if (!ok) break;
-            umma_commit(PLANES == 2 ? &small_full_bar[tb] : &acc_full_bar[tb]);
         }
         // Drain: every MMA this thread issued must retire before TMEM is freed.
         umma_commit(drain_bar);
@@ -311,86 +298,68 @@ __global__ void __launch_bounds__(192, 1)
         // ------------------------------------------------------------ epilogue
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
         const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        int local = 0;
-        int chunk = 0;
+        int buf = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-            const int tb = local & 1;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
             int m0, n0;
             tile_coords(t, p, BN, &m0, &n0);
             const int row = m0 + quarter * 32 + lane;
             const bool row_ok = row < p.m;
             float* crow = p.c + static_cast<long long>(row) * p.ldc;
-            const int nchunks = min(BN / 32, (p.n - n0 + 31) / 32);
             if constexpr (PLANES == 2) {
-                // Round-to-nearest FP32 sum of the big-accumulator chunks, in registers.
-                float sum[128];
+                // Round-to-nearest FP32 sum of the K chunks, in registers: this warp owns
+                // columns [half * BN/2, (half + 1) * BN/2) of the tile.
+                constexpr int kCols = BN / 2;
+                const int half = (warp - 2) >> 2;
+                float sum[kCols];
 #pragma unroll
-                for (int j = 0; j < 128; ++j) sum[j] = 0.0f;
+                for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
                 const int n_chunks = (p.num_kb + kChunkKb - 1) / kChunkKb;
-                for (int c = 0; c < n_chunks; ++c, ++chunk) {
-                    const int cb = chunk & 1;
-                    if (!mbar_wait_bounded(&acc_full_bar[cb], (chunk >> 1) & 1, limit, abort_flag)) {
+                for (int c = 0; c < n_chunks; ++c, ++buf) {
+                    const int b = buf & 1;
+                    if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
                         report_status(kStatusTimeoutEpilogue, abort_flag);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint32_t r[32];
-                        tmem_ld_32x32b_x32(tmem_base + lane_base + cb * 128 + q * 32, r);
+                    for (int q = 0; q < kCols / 16; ++q) {
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16(tmem_base + lane_base + b * BN + half * kCols + q * 16, r);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) sum[q * 32 + j] += __uint_as_float(r[j]);
+                        for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
                     }
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty_bar[cb]);
+                    if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
                 }
                 if (!ok) break;
-                if (!mbar_wait_bounded(&small_full_bar[tb], (local >> 1) & 1, limit, abort_flag)) {
-                    report_status(kStatusTimeoutEpilogue, abort_flag);
-                    break;
-                }
-                tc_fence_after();
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(tmem_base + lane_base + 256 + tb * 128 + q * 32, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) sum[q * 32 + j] += __uint_as_float(r[j]);
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&small_empty_bar[tb]);
                 if (row_ok) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        if (q < nchunks) {
-                            float v[32];
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] = sum[q * 32 + j];
-                            store_row_chunk(crow, n0 + q * 32, v, p);
-                        }
+                    for (int q = 0; q < kCols / 32; ++q) {
+                        const int col0 = n0 + half * kCols + q * 32;
+                        if (col0 < p.n) store_row_chunk(crow, col0, &sum[q * 32], p);
                     }
                 }
             } else {
-                if (!mbar_wait_bounded(&acc_full_bar[tb], (local >> 1) & 1, limit, abort_flag)) {
+                const int b = buf & 1;
+                if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
                     report_status(kStatusTimeoutEpilogue, abort_flag);
                     break;
                 }
                 tc_fence_after();
+                const int nchunks = min(BN / 32, (p.n - n0 + 31) / 32);
                 for (int q = 0; q < nchunks; ++q) {
                     uint32_t r[32];
-                    tmem_ld_32x32b_x32(tmem_base + lane_base + tb * BN + q * 32, r);
+                    tmem_ld_32x32b_x32(tmem_base + lane_base + b * BN + q * 32, r);
                     tmem_ld_wait();
                     if (q == nchunks - 1) {
                         // Accumulator fully read: hand it back to the MMA issuer.
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty_bar[tb]);
+                        if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
                     }
                     if (row_ok) {
                         float v[32];
@@ -399,6 +368,7 @@ __global__ void __launch_bounds__(192, 1)
                         store_row_chunk(crow, n0 + q * 32, v, p);
                     }
                 }
+                ++buf;
             }
         }
     }

@@ -228,22 +228,8 @@ mfb_status_t plan_run(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, co
         case kPathGemv: return multiply ? gemv_launch(d, stream, a, b, c, bias, plan->ws, plan->ws_bytes) : MFB_OK;
         default: break;
     }
-    const size_t need = tc_workspace_bytes(d, a, b, false);
-    if (need > plan->ws_bytes) {
-        // Only a TF32 plan given unaligned operands lands here: grow once, outside capture.
-        if (stream_capturing(stream))
-            return fail(MFB_EINVAL, "TF32 plan got operands that are not 16-byte aligned during graph capture");
-        MFB_CUDA_TRY(cudaStreamSynchronize(stream), "plan workspace resize sync");
-        if (plan->ws) cudaFree(plan->ws);
-        plan->ws = nullptr;
-        plan->ws_bytes = 0;
-        cudaError_t e = cudaMalloc(&plan->ws, need);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            return cuda_fail(e, "plan workspace cudaMalloc");
-        }
-        plan->ws_bytes = need;
-    }
+    // The plan's scratch was sized for this shape at creation; execute allocates nothing.
+    if (tc_workspace_bytes(d) > plan->ws_bytes) return fail(MFB_EINVAL, "plan scratch does not cover this shape");
     return tc_gemm(d, plan->cfg, stream, a, b, c, bias, plan->ws, plan->ws_bytes, phases, plan->sm_limit);
 }
 
@@ -314,7 +300,7 @@ MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream_h, const mfb_gemm
     }
     TcConfig cfgs[4];
     if (tc_candidates(d, cfgs, 4) == 0) return fail(MFB_EUNSUPPORTED, "no tcgen05 configuration");
-    const size_t need = tc_workspace_bytes(d, a, b, false);
+    const size_t need = tc_workspace_bytes(d);
     void* ws = nullptr;
     MFB_TRY(stream_workspace(device, stream, need, &ws));
     return tc_gemm(d, cfgs[0], stream, a, b, c, bias, ws, need);
@@ -376,9 +362,7 @@ MFB_API mfb_status_t mfb_plan_create(int device, const mfb_gemm_desc* desc, mfb_
         plan->n_candidates = tc_candidates(probe, plan->candidates, 16);
         if (plan->n_candidates == 0) return fail(MFB_EUNSUPPORTED, "no tcgen05 configuration");
         plan->cfg = plan->candidates[0];
-        // TF32 operands are used in place when 16-byte aligned with ld % 4 == 0; scratch
-        // covers the repack of any operand whose ld rules that out.
-        need = tc_workspace_bytes(probe, nullptr, nullptr, true);
+        need = tc_workspace_bytes(probe);  // operand planes: hi/lo (strict) or rounded TF32
     } else if (plan->path == kPathGemv) {
         need = gemv_workspace_bytes(probe);
     }
@@ -433,7 +417,7 @@ MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream_h, const
     MFB_TRY(validate_desc(&d, a, b, scratch_c, nullptr, true));
     DeviceGuard guard;
     MFB_TRY(select_device(plan->device));
-    const size_t need = tc_workspace_bytes(d, a, b, false);
+    const size_t need = tc_workspace_bytes(d);
     if (need > plan->ws_bytes) return fail(MFB_EINVAL, "plan workspace does not cover these operands");
     cudaEvent_t e0, e1;
     MFB_CUDA_TRY(cudaEventCreate(&e0), "event create");

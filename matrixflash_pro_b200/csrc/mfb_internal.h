@@ -66,19 +66,13 @@ struct TcConfig {
 // Admissible tile configurations for a problem, best-guess first.
 int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out);
 
-struct OperandLayout {
-    int rows = 0, cols = 0;     // stored matrix
-    long long ld = 0;           // elements
-    size_t plane_floats = 0;    // floats per split plane (0 when used in place)
-};
+// Scratch the tcgen05 path needs for `d`: hi/lo planes of A and B (strict) or one
+// rounded TF32 plane of each (TF32), rows padded to 16 bytes.
+size_t tc_workspace_bytes(const mfb_gemm_desc& d);
 
-// Scratch the tcgen05 path needs for `d` (split planes or repacked operands).
-size_t tc_workspace_bytes(const mfb_gemm_desc& d, const float* a, const float* b, bool assume_aligned_inputs);
-
-// Runs the tcgen05 GEMM on `stream`: kPhasePrepare launches the split/pack prepass of
+// Runs the tcgen05 GEMM on `stream`: kPhasePrepare launches the split/round prepass of
 // the operands into `workspace`, kPhaseMultiply the GEMM kernel on the prepared
-// operands (a/b are still needed for operands used in place). sm_limit > 0 caps the
-// persistent grid.
+// operands. sm_limit > 0 caps the persistent grid.
 enum { kPhasePrepare = 1, kPhaseMultiply = 2, kPhaseAll = 3 };
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,

@@ -1,0 +1,100 @@
+"""CPU tier: the multi-GPU row split on 2 gloo ranks (no GPU).
+
+Checks the host logic of matrixflash_pro_b200.distributed: row partition, K panels,
+the broadcast of B panels from rank 0, and the per-panel accumulation rule
+(beta on the first panel, 1 afterwards). The per-panel GEMM is the oracle here (test
+infrastructure), standing in for the tcgen05 plan that runs on the GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from matrixflash_pro_b200.distributed import k_panels, row_partition, run_schedule, schedule
+
+
+def test_row_partition_covers_rows_once():
+    for m in (1, 7, 8192, 32768, 1000):
+        for world in (1, 2, 3, 4, 8):
+            spans = [row_partition(m, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == m
+            for (b0, e0), (b1, e1) in zip(spans, spans[1:]):
+                assert e0 == b1 and b0 <= e0
+    with pytest.raises(Exception):
+        row_partition(10, 2, 2)
+
+
+def test_k_panels():
+    assert k_panels(4096, 1) == [(0, 4096)]
+    assert k_panels(4096, 8) == [(0, 512), (512, 4096)]
+    assert k_panels(32768, 2) == [(0, 4096), (4096, 32768)]
+    assert k_panels(40, 4) == [(0, 40)]
+    for k in (100, 4097, 5000):
+        p = k_panels(k, 4)
+        assert p[0][0] == 0 and p[-1][1] == k and all(a < b for a, b in p) and p[0][1] % 32 == 0
+
+
+def test_schedule_betas_and_sm_limits():
+    s = schedule(4096, 4, 0.5, 16, 148)
+    assert s.betas == [0.5, 1.0] and s.sm_limits == [132, None]
+    s1 = schedule(4096, 1, 0.5, 16, 148)
+    assert s1.betas == [0.5] and s1.sm_limits == [None]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, result_dir):
+    import oracle
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m, n, k, ldb = 37, 29, 300, 31
+        alpha, beta = 0.5, 1.0
+        rng = np.random.default_rng(0)
+        A_full = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        B_full = rng.standard_normal((k, ldb)).astype(np.float32)
+        C_full = rng.standard_normal((m, n)).astype(np.float32)
+        r0, r1 = row_partition(m, world, rank)
+        A = A_full[r0:r1].copy()
+        C = C_full[r0:r1].copy()
+        B = torch.from_numpy(B_full.copy()) if rank == 0 else torch.full((k, ldb), float("nan"))
+        sched = schedule(k, world, beta, 16, 148)
+
+        def panel_gemm(i, panel, pbeta, sm_limit):
+            k0, k1 = panel
+            b_panel = B[k0:k1].numpy()
+            a_panel = np.ascontiguousarray(A[:, k0:k1])
+            oracle.gemm_f32(r1 - r0, n, k1 - k0, a_panel, k1 - k0, b_panel, ldb, C, n, alpha, pbeta)
+
+        run_schedule(sched, lambda k0, k1: B[k0:k1], panel_gemm)
+        np.save(os.path.join(result_dir, f"c{rank}.npy"), C)
+        np.save(os.path.join(result_dir, f"b{rank}.npy"), B.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_split_with_panel_broadcast_two_gloo_ranks(tmp_path):
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    import oracle
+    m, n, k, ldb = 37, 29, 300, 31
+    rng = np.random.default_rng(0)
+    A_full = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    B_full = rng.standard_normal((k, ldb)).astype(np.float32)
+    C_full = rng.standard_normal((m, n)).astype(np.float32)
+    got = np.concatenate([np.load(tmp_path / f"c{r}.npy") for r in range(world)])
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"b{r}.npy"), B_full), "B reached every rank"
+    ref64 = 0.5 * (A_full.astype(np.float64) @ B_full[:, :n].astype(np.float64)) + C_full
+    ref32 = C_full.copy()
+    oracle.gemm_f32(m, n, k, A_full, k, B_full, ldb, ref32, n, 0.5, 1.0)
+    assert oracle.normwise_rel(got, ref64) <= max(1e-6, oracle.normwise_rel(ref32, ref64))
