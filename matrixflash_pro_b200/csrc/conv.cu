@@ -1,18 +1,97 @@
 // conv2d forward (NCHW cross-correlation), replacing conv2d / conv2d_kernel of the
 // reference (src/nn/conv.cu:22-49,110-163).
 //
-// Direct kernel: one thread per output pixel and a block-shared copy of the
-// filter's weights; taps in the reference's order (channel -> kh -> kw, bias
-// first, FMA), so results match the reference kernel's arithmetic exactly.
+// Stride 1 (the reference's bench shapes): implicit GEMM on tcgen05 (conv_tc.cuh)
+// after a prepass that writes the zero-padded input with channels innermost, and the
+// per-tap weights, as TF32 planes (hi/lo for strict FP32, one rounded plane for TF32).
+// Other strides: a direct kernel, one thread per output with the filter staged in
+// shared memory and the reference's tap order (channel -> kh -> kw, FMA).
+#include "conv_tc.cuh"
 #include "mfb_internal.h"
 
 #include <algorithm>
+#include <mutex>
 
 namespace mfb {
 
 namespace {
 
 constexpr int kConvThreads = 256;
+
+__device__ __forceinline__ float conv_round_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// Writes 4 consecutive floats as TF32 planes: hi = tf32(v), lo = tf32(v - hi) (lo may be null).
+__device__ __forceinline__ void write_planes4(float* hi, float* lo, long long off, float v0, float v1, float v2,
+                                              float v3) {
+    const float v[4] = {v0, v1, v2, v3};
+    float h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        h[i] = conv_round_tf32(v[i]);
+        l[i] = conv_round_tf32(v[i] - h[i]);
+    }
+    *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
+    if (lo) *reinterpret_cast<float4*>(lo + off) = make_float4(l[0], l[1], l[2], l[3]);
+}
+
+// x (N,C,H,W) -> X [N][Hp*Wp][Cp]: zero border of `pad`, zero channels in [C, Cp).
+// grid (ceil(Hp*Wp / 64), ceil(Cp / 32), N): a 32-channel x 64-position tile is read
+// along positions (coalesced in W) and written as 128-byte channel rows.
+__global__ void __launch_bounds__(256) conv_pack_input_kernel(const float* __restrict__ x, int c, int h, int w,
+                                                              int pad, int cp, int hp, int wp,
+                                                              float* __restrict__ hi, float* __restrict__ lo) {
+    __shared__ float tile[32][65];
+    const int npos = hp * wp;
+    const int pos0 = blockIdx.x * 64;
+    const int c0 = blockIdx.y * 32;
+    const int img = blockIdx.z;
+    for (int i = threadIdx.x; i < 32 * 64; i += blockDim.x) {
+        const int cc = i / 64, pp = i % 64;
+        const int pos = pos0 + pp, ch = c0 + cc;
+        float v = 0.0f;
+        if (pos < npos && ch < c) {
+            const int ih = pos / wp - pad, iw = pos % wp - pad;
+            if (ih >= 0 && ih < h && iw >= 0 && iw < w)
+                v = __ldg(x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + iw);
+        }
+        tile[cc][pp] = v;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
+        const int pp = i / 8, q = i % 8;
+        const int pos = pos0 + pp, ch = c0 + 4 * q;
+        if (pos < npos && ch < cp) {
+            const long long off = (static_cast<long long>(img) * npos + pos) * cp + ch;
+            write_planes4(hi, lo, off, tile[4 * q][pp], tile[4 * q + 1][pp], tile[4 * q + 2][pp], tile[4 * q + 3][pp]);
+        }
+    }
+}
+
+// w (K,C,R,S) -> W [R*S][K][Cp].
+__global__ void conv_pack_weights_kernel(const float* __restrict__ wt, int kf, int c, int r, int s, int cp,
+                                         float* __restrict__ hi, float* __restrict__ lo) {
+    const int groups = cp / 4;
+    const long long total = static_cast<long long>(r) * s * kf * groups;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int g = static_cast<int>(idx % groups);
+        const long long r1 = idx / groups;
+        const int f = static_cast<int>(r1 % kf);
+        const int tap = static_cast<int>(r1 / kf);
+        const int rr = tap / s, ss = tap % s;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int ch = 4 * g + i;
+            v[i] = ch < c ? __ldg(wt + ((static_cast<long long>(f) * c + ch) * r + rr) * s + ss) : 0.0f;
+        }
+        write_planes4(hi, lo, idx * 4, v[0], v[1], v[2], v[3]);
+    }
+}
 
 // grid: (ceil(P*Q / 256), K, N). Weights of filter blockIdx.y are staged in shared memory.
 __global__ void __launch_bounds__(kConvThreads) conv2d_direct_kernel(const float* __restrict__ x,
@@ -48,16 +127,8 @@ __global__ void __launch_bounds__(kConvThreads) conv2d_direct_kernel(const float
     y[(static_cast<long long>(nimg) * K + f) * P * Q + pix] = sum;
 }
 
-}  // namespace
-
-mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
-                           int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
-                           int precision) {
-    (void)device;
-    (void)precision;
-    const int P = (h + 2 * pad - r) / stride + 1;
-    const int Q = (w + 2 * pad - s) / stride + 1;
-    if (n == 0 || P <= 0 || Q <= 0) return MFB_OK;
+mfb_status_t conv2d_direct(cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s, int stride, int pad,
+                           int P, int Q, const float* x, const float* wgt, const float* bias, float* y) {
     const long long taps = static_cast<long long>(c) * r * s;
     const size_t smem = static_cast<size_t>(taps) * 4;
     if (smem > 200 * 1024) return fail(MFB_EUNSUPPORTED, "conv2d filter too large for the direct kernel");
@@ -69,6 +140,146 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
     dim3 grid((P * Q + kConvThreads - 1) / kConvThreads, k, n);
     conv2d_direct_kernel<<<grid, kConvThreads, smem, stream>>>(x, wgt, bias, y, c, h, w, k, r, s, P, Q, stride, pad);
     MFB_CUDA_TRY(cudaGetLastError(), "conv2d launch");
+    return MFB_OK;
+}
+
+// ------------------------------------------------------------------------------------ tcgen05 conv table
+struct ConvEntry {
+    int bn, planes;
+    const void* fn;
+    int smem, threads;
+};
+
+template <int BN, int PLANES>
+ConvEntry make_conv_entry() {
+    using P = ConvProblem<BN, PLANES>;
+    using L = TcLayout<P>;
+    return ConvEntry{BN, PLANES, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes, L::kThreads};
+}
+
+const ConvEntry* conv_table(int* count) {
+    static const ConvEntry table[] = {
+        make_conv_entry<16, 2>(), make_conv_entry<32, 2>(), make_conv_entry<64, 2>(), make_conv_entry<128, 2>(),
+        make_conv_entry<256, 2>(), make_conv_entry<16, 1>(), make_conv_entry<32, 1>(), make_conv_entry<64, 1>(),
+        make_conv_entry<128, 1>(), make_conv_entry<256, 1>(),
+    };
+    *count = static_cast<int>(sizeof(table) / sizeof(table[0]));
+    return table;
+}
+
+// Narrowest filter tile that covers K (one filter tile per position tile when K <= 256).
+const ConvEntry* pick_conv(int kf, int planes) {
+    int count = 0;
+    const ConvEntry* t = conv_table(&count);
+    const ConvEntry* best = nullptr;
+    for (int i = 0; i < count; ++i) {
+        if (t[i].planes != planes) continue;
+        if (t[i].bn >= kf && (!best || t[i].bn < best->bn)) best = &t[i];
+    }
+    if (!best)
+        for (int i = 0; i < count; ++i)
+            if (t[i].planes == planes && (!best || t[i].bn > best->bn)) best = &t[i];
+    return best;
+}
+
+long long round_up64(long long v) { return (v + 63) / 64 * 64; }
+
+}  // namespace
+
+size_t conv2d_workspace_bytes(int n, int c, int h, int w, int k, int r, int s, int stride, int pad, int precision) {
+    if (stride != 1) return 0;
+    const long long planes = precision == MFB_PRECISION_FP32 ? 2 : 1;
+    const long long cp = (c + 3) / 4 * 4;
+    const long long a = round_up64(static_cast<long long>(n) * (h + 2 * pad) * (w + 2 * pad) * cp);
+    const long long b = round_up64(static_cast<long long>(r) * s * k * cp);
+    return static_cast<size_t>(planes * (a + b) * 4);
+}
+
+mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
+                           int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
+                           int precision) {
+    const int P = (h + 2 * pad - r) / stride + 1;
+    const int Q = (w + 2 * pad - s) / stride + 1;
+    if (n == 0 || P <= 0 || Q <= 0) return MFB_OK;
+    if (stride != 1) return conv2d_direct(stream, n, c, h, w, k, r, s, stride, pad, P, Q, x, wgt, bias, y);
+
+    const int planes = precision == MFB_PRECISION_FP32 ? 2 : 1;
+    const int cp = (c + 3) / 4 * 4;
+    const int hp = h + 2 * pad, wp = w + 2 * pad;
+    const long long npos = static_cast<long long>(hp) * wp;
+    if (n > 65535 || npos > 0x7fffffffLL) return fail(MFB_EUNSUPPORTED, "conv2d input too large");
+    const ConvEntry* e = pick_conv(k, planes);
+    if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 conv configuration");
+
+    const size_t need = conv2d_workspace_bytes(n, c, h, w, k, r, s, stride, pad, precision);
+    void* ws = nullptr;
+    MFB_TRY(stream_workspace(device, stream, need, &ws));
+    const long long a_plane = round_up64(static_cast<long long>(n) * npos * cp);
+    const long long b_plane = round_up64(static_cast<long long>(r) * s * k * cp);
+    float* a_hi = static_cast<float*>(ws);
+    float* a_lo = planes == 2 ? a_hi + a_plane : nullptr;
+    float* b_hi = a_hi + planes * a_plane;
+    float* b_lo = planes == 2 ? b_hi + b_plane : nullptr;
+
+    dim3 pgrid(static_cast<unsigned>((npos + 63) / 64), static_cast<unsigned>((cp + 31) / 32), n);
+    conv_pack_input_kernel<<<pgrid, 256, 0, stream>>>(x, c, h, w, pad, cp, hp, wp, a_hi, a_lo);
+    MFB_CUDA_TRY(cudaGetLastError(), "conv input prepass launch");
+    const long long wgroups = static_cast<long long>(r) * s * k * (cp / 4);
+    conv_pack_weights_kernel<<<static_cast<int>(std::min<long long>((wgroups + 255) / 256, 148LL * 4)), 256, 0,
+                               stream>>>(wgt, k, c, r, s, cp, b_hi, b_lo);
+    MFB_CUDA_TRY(cudaGetLastError(), "conv weight prepass launch");
+
+    // X: dims (Cp, Hp*Wp, N, planes); W: dims (Cp, K, R*S, planes); boxes of 32 channels.
+    CUtensorMap map_a, map_b;
+    {
+        const uint64_t dims[4] = {static_cast<uint64_t>(cp), static_cast<uint64_t>(npos), static_cast<uint64_t>(n),
+                                  static_cast<uint64_t>(planes)};
+        const uint64_t strides[3] = {static_cast<uint64_t>(cp) * 4, static_cast<uint64_t>(npos) * cp * 4,
+                                     static_cast<uint64_t>(a_plane) * 4};
+        const uint32_t box[4] = {32, static_cast<uint32_t>(kTcBM), 1, static_cast<uint32_t>(planes)};
+        MFB_TRY(encode_tensor_map(&map_a, a_hi, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    {
+        const uint64_t dims[4] = {static_cast<uint64_t>(cp), static_cast<uint64_t>(k), static_cast<uint64_t>(r) * s,
+                                  static_cast<uint64_t>(planes)};
+        const uint64_t strides[3] = {static_cast<uint64_t>(cp) * 4, static_cast<uint64_t>(k) * cp * 4,
+                                     static_cast<uint64_t>(b_plane) * 4};
+        const uint32_t box[4] = {32, static_cast<uint32_t>(e->bn), 1, static_cast<uint32_t>(planes)};
+        MFB_TRY(encode_tensor_map(&map_b, b_hi, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+
+    ConvTcParams p{};
+    p.n_img = n;
+    p.c = c;
+    p.h = h;
+    p.w = w;
+    p.kf = k;
+    p.r = r;
+    p.s = s;
+    p.pad = pad;
+    p.hp = hp;
+    p.wp = wp;
+    p.p_out = P;
+    p.q_out = Q;
+    p.ncb = (cp + 31) / 32;
+    p.num_kb = r * s * p.ncb;
+    p.tiles_pos = static_cast<int>((static_cast<long long>(P) * wp + kTcBM - 1) / kTcBM);
+    p.tiles_f = (k + e->bn - 1) / e->bn;
+    p.y = y;
+    p.bias = bias;
+    p.wait_limit_ns = wait_limit_ns();
+    const long long tiles = static_cast<long long>(n) * p.tiles_pos * p.tiles_f;
+    if (tiles > 0x7fffffffLL) return fail(MFB_EINVAL, "conv2d has too many output tiles");
+    const int grid = static_cast<int>(std::min<long long>(tiles, sm_count(device)));
+    static std::mutex attr_mutex;
+    {
+        std::lock_guard<std::mutex> lock(attr_mutex);
+        MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem),
+                     "conv smem attribute");
+    }
+    void* args[] = {&map_a, &map_b, &p};
+    MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(grid), dim3(e->threads), args, static_cast<size_t>(e->smem), stream),
+                 "tcgen05 conv launch");
     return MFB_OK;
 }
 

@@ -122,10 +122,35 @@ mfb_status_t encode_operand(CUtensorMap* map, const float* base, int rows, int c
     return MFB_OK;
 }
 
+}  // namespace
+
+mfb_status_t encode_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(MFB_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    cuuint64_t d[5];
+    cuuint64_t st[4];
+    cuuint32_t b[5];
+    cuuint32_t es[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) st[i] = strides_bytes[i];
+    }
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st,
+                    b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(MFB_ECUDA, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
+    return MFB_OK;
+}
+
+namespace {
+
 // ------------------------------------------------------------------------------------
 // Kernel table
 // ------------------------------------------------------------------------------------
-using TcKernel = void (*)(CUtensorMap, CUtensorMap, GemmTcParams);
 
 struct TcEntry {
     int bn, stages, planes, a_mn, b_mn;
@@ -136,9 +161,9 @@ struct TcEntry {
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
 TcEntry make_entry() {
-    using L = GemmTcSmem<BN, STAGES, PLANES>;
-    return TcEntry{BN, STAGES, PLANES, A_MN, B_MN,
-                   reinterpret_cast<const void*>(&gemm_tf32_tc_kernel<BN, STAGES, PLANES, A_MN, B_MN>), L::kBytes,
+    using P = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>;
+    using L = TcLayout<P>;
+    return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes,
                    L::kThreads};
 }
 
@@ -212,7 +237,7 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
     int count = 0;
     const TcEntry* t = kernel_table(&count);
     const int sms = 148;
-    const long long tiles_m = (d.m + kBM - 1) / kBM;
+    const long long tiles_m = (d.m + kTcBM - 1) / kTcBM;
     // Widest tile that still fills the GPU goes first; the rest follow by width.
     int order[16];
     int n_ok = 0;
@@ -306,7 +331,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         const PreparedOperand& A = ops[0];
         // K-major A: box 32 (K) x 128 (M); MN-major A: box 32 (M) x 32 (K).
         MFB_TRY(encode_operand(&map_a, A.base, A.rows, A.cols, A.ld, cfg.planes, A.plane_stride, 32,
-                               cfg.a_mn ? 32 : kBM, cfg.a_mn != 0));
+                               cfg.a_mn ? 32 : kTcBM, cfg.a_mn != 0));
         const PreparedOperand& B = ops[1];
         MFB_TRY(encode_operand(&map_b, B.base, B.rows, B.cols, B.ld, cfg.planes, B.plane_stride, 32,
                                cfg.b_mn ? 32 : cfg.bn, cfg.b_mn != 0));
@@ -317,7 +342,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     p.n = d.n;
     p.k = d.k;
     p.num_kb = (d.k + kBK - 1) / kBK;
-    p.tiles_m = (d.m + kBM - 1) / kBM;
+    p.tiles_m = (d.m + kTcBM - 1) / kTcBM;
     p.tiles_n = (d.n + cfg.bn - 1) / cfg.bn;
     p.group_m = 16;
     p.c = c;

@@ -78,6 +78,11 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
                      int phases = kPhaseAll, int sm_limit = 0);
 
+// cuTensorMapEncodeTiled for FP32 tensors of rank <= 5 (no interleave, L2 256B promotion,
+// zero fill out of bounds); strides_bytes has rank - 1 entries.
+mfb_status_t encode_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
 // C = beta * C, then the epilogue; the k == 0 / alpha == 0 path.
 mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c, const float* bias);
 

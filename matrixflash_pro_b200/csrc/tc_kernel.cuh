@@ -1,0 +1,288 @@
+// Persistent tcgen05 mainloop shared by the GEMM and the implicit-GEMM conv2d.
+//
+// One CTA per SM walks 128 x BN output tiles round-robin:
+//   warp 0      TMA producer: one elected lane fills a STAGES-deep ring of
+//               shared-memory stages (Prob::load), running ahead across tiles.
+//   warp 1      allocates 2 x BN TMEM columns; one elected lane issues
+//               tcgen05.mma kind::tf32 (Prob::a_desc / b_desc) and releases each stage
+//               with tcgen05.commit.
+//   warps 2..   epilogue: tcgen05.ld of the FP32 accumulator and Prob::store.
+//
+// PLANES = 1 (TF32): one TF32 pass per K step into a 128 x BN FP32 accumulator; two
+// accumulators alternate between tiles so the epilogue of tile i overlaps the MMAs of
+// tile i+1 (4 epilogue warps, one per TMEM sub-partition).
+//
+// PLANES = 2 (strict FP32): each operand arrives as a (hi, lo) pair of TF32 planes
+// (x = hi + lo + O(2^-22 |x|)); every K step issues lo*hi, hi*lo, then hi*hi. The
+// tensor core folds each MMA into its FP32 accumulator with a truncating
+// (round-toward-zero) add, so one accumulator over all of K drifts by ~K/8 ulps
+// (1.4e-5 normwise at K=2048, measured). The accumulator is therefore restarted every
+// kChunkKb K blocks (64 of K) and the epilogue warps fold each finished chunk into FP32
+// registers with round-to-nearest adds; two chunk buffers alternate so the MMAs never
+// wait for the fold. 8 epilogue warps: two per TMEM sub-partition, each owning BN/2
+// columns of its 32 rows in registers.
+//
+// Every mbarrier wait is bounded by p.wait_limit_ns of %globaltimer; a wait that runs
+// out records a bit in mfb::g_status, asks the other roles to stop, drains in-flight
+// TMA copies and MMAs (again bounded) and frees TMEM before the CTA exits.
+#pragma once
+
+#include "mfb_device.cuh"
+
+#include <cuda.h>
+
+namespace mfb {
+
+constexpr int kTcBM = 128;
+constexpr int kChunkKb = 2;  // strict mode: the accumulator restarts every 2 K blocks
+
+__device__ __forceinline__ float apply_epilogue_op(float v, const float* bias, int col, int epilogue) {
+    if (epilogue != 0) {
+        v += bias[col];
+        if (epilogue == 2) {
+            v = v > 0.0f ? v : 0.0f;
+        } else if (epilogue == 3) {
+            const float x3 = v * v * v;
+            v = 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * x3)));
+        }
+    }
+    return v;
+}
+
+template <class Prob>
+struct TcLayout {
+    static constexpr int kStageBytes = Prob::kATileBytes + Prob::kBTileBytes;
+    static constexpr int kBarrierOffset = Prob::STAGES * kStageBytes;
+    static constexpr int kBytes = kBarrierOffset + 256 + 1024;  // barriers + 1 KiB alignment slack
+    static constexpr int kTmemCols = 2 * Prob::BN < 32 ? 32 : 2 * Prob::BN;
+    static constexpr int kEpiWarps = Prob::PLANES == 2 ? 8 : 4;
+    static constexpr int kThreads = 64 + 32 * kEpiWarps;
+};
+
+// Loads `count` (8 or 16) accumulator columns of this warp's 32 lanes.
+template <int COUNT>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* out) {
+    if constexpr (COUNT == 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(taddr, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) out[j] = __uint_as_float(r[j]);
+    } else {
+        uint32_t r[8];
+        tmem_ld_32x32b_x8(taddr, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) out[j] = __uint_as_float(r[j]);
+    }
+}
+
+template <class Prob>
+__global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
+    tc_persistent_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                         const typename Prob::Params p) {
+    using L = TcLayout<Prob>;
+    constexpr int BN = Prob::BN;
+    constexpr int STAGES = Prob::STAGES;
+    constexpr int PLANES = Prob::PLANES;
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "BN");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* acc_full_bar = empty_bar + STAGES;  // [2] tile (tf32) or K-chunk (strict) buffers
+    uint64_t* acc_empty_bar = acc_full_bar + 2;   // [2]
+    uint64_t* drain_bar = acc_empty_bar + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int num_tiles = Prob::num_tiles(p);
+    const int num_kb = Prob::num_kb(p);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full_bar[b], 1);
+            mbar_init(&acc_empty_bar[b], L::kEpiWarps);  // one arrival per epilogue warp
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, L::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint64_t limit = p.wait_limit_ns;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------ TMA producer
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            const typename Prob::Tile tile = Prob::tile(p, t);
+            for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                const int s = it % STAGES;
+                if (!mbar_wait_bounded(&empty_bar[s], ((it / STAGES) & 1) ^ 1, limit, abort_flag)) {
+                    report_status(kStatusTimeoutProducer, abort_flag);
+                    ok = false;
+                    break;
+                }
+                uint8_t* a_tile = smem + s * L::kStageBytes;
+                mbar_arrive_expect_tx(&full_bar[s], L::kStageBytes);
+                Prob::load(p, &tmap_a, &tmap_b, a_tile, a_tile + Prob::kATileBytes, &full_bar[s], tile, kb);
+            }
+        }
+        // Drain: every issued copy must land before this CTA's shared memory goes away.
+        for (int j = it - STAGES < 0 ? 0 : it - STAGES; j < it; ++j) {
+            if (!mbar_wait_drain(&full_bar[j % STAGES], (j / STAGES) & 1, limit)) {
+                report_status(kStatusTimeoutDrain, nullptr);
+                break;
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------ MMA issuer
+        constexpr uint32_t idesc = umma_idesc_tf32(kTcBM, BN, Prob::A_MN, Prob::B_MN);
+        // Accumulator buffers are handed out per tile (tf32) or per K chunk (strict).
+        const int kb_per_buf = PLANES == 2 ? kChunkKb : 0x7fffffff;
+        int it = 0;   // K blocks consumed (stage ring position)
+        int buf = 0;  // accumulator buffers used so far
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            uint32_t d_tmem = 0;
+            uint32_t acc = 0;
+            for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                if (kb % kb_per_buf == 0) {
+                    const int b = buf & 1;
+                    if (!mbar_wait_bounded(&acc_empty_bar[b], ((buf >> 1) & 1) ^ 1, limit, abort_flag)) {
+                        report_status(kStatusTimeoutMma, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    d_tmem = tmem_base + b * BN;
+                    acc = 0;
+                }
+                const int s = it % STAGES;
+                if (!mbar_wait_bounded(&full_bar[s], (it / STAGES) & 1, limit, abort_flag)) {
+                    report_status(kStatusTimeoutMma, abort_flag);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+                const uint32_t b_addr = a_addr + Prob::kATileBytes;
+#pragma unroll
+                for (int ks = 0; ks < Prob::kKSteps; ++ks) {
+                    const uint64_t a_hi = Prob::a_desc(a_addr, 0, ks);
+                    const uint64_t b_hi = Prob::b_desc(b_addr, 0, ks);
+                    if (PLANES == 2) {
+                        umma_tf32(d_tmem, Prob::a_desc(a_addr, 1, ks), b_hi, idesc, acc);
+                        acc = 1;
+                        umma_tf32(d_tmem, a_hi, Prob::b_desc(b_addr, 1, ks), idesc, 1);
+                    }
+                    umma_tf32(d_tmem, a_hi, b_hi, idesc, acc);
+                    acc = 1;
+                }
+                umma_commit(&empty_bar[s]);
+                if (kb % kb_per_buf == kb_per_buf - 1 || kb == num_kb - 1) {
+                    umma_commit(&acc_full_bar[buf & 1]);
+                    ++buf;
+                }
+            }
+        }
+        // Drain: every MMA this thread issued must retire before TMEM is freed.
+        umma_commit(drain_bar);
+        if (!mbar_wait_drain(drain_bar, 0, limit)) report_status(kStatusTimeoutDrain, nullptr);
+    } else if (warp >= 2) {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const int row = quarter * 32 + lane;  // row within the tile
+        int buf = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            const typename Prob::Tile tile = Prob::tile(p, t);
+            const int valid = Prob::valid_cols(p, tile);
+            if constexpr (PLANES == 2) {
+                // Round-to-nearest FP32 sum of the K chunks, in registers: this warp owns
+                // columns [half * BN/2, (half + 1) * BN/2) of the tile.
+                constexpr int kCols = BN / 2;
+                constexpr int kStep = kCols % 16 == 0 ? 16 : 8;
+                const int half = (warp - 2) >> 2;
+                float sum[kCols];
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
+                const int n_chunks = (num_kb + kChunkKb - 1) / kChunkKb;
+                for (int c = 0; c < n_chunks; ++c, ++buf) {
+                    const int b = buf & 1;
+                    if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
+                        report_status(kStatusTimeoutEpilogue, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int q = 0; q < kCols / kStep; ++q) {
+                        float v[kStep];
+                        tmem_load_cols<kStep>(tmem_base + lane_base + b * BN + half * kCols + q * kStep, v);
+#pragma unroll
+                        for (int j = 0; j < kStep; ++j) sum[q * kStep + j] += v[j];
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
+                }
+                if (!ok) break;
+#pragma unroll
+                for (int q = 0; q < kCols / kStep; ++q) {
+                    const int col0 = half * kCols + q * kStep;
+                    if (col0 < valid) Prob::template store<kStep>(p, tile, row, col0, &sum[q * kStep]);
+                }
+            } else {
+                const int b = buf & 1;
+                if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
+                    report_status(kStatusTimeoutEpilogue, abort_flag);
+                    break;
+                }
+                tc_fence_after();
+                const int nq = (min(valid, BN) + 15) / 16;
+                for (int q = 0; q < nq; ++q) {
+                    float v[16];
+                    tmem_load_cols<16>(tmem_base + lane_base + b * BN + q * 16, v);
+                    if (q == nq - 1) {
+                        // Accumulator fully read: hand it back to the MMA issuer.
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
+                    }
+                    Prob::template store<16>(p, tile, row, q * 16, v);
+                }
+                ++buf;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+}  // namespace mfb
