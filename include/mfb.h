@@ -114,6 +114,22 @@ MFB_API mfb_status_t mfb_cuda_device_count(int* count);
 MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
                                const float* b, float* c, const float* bias);
 
+/* ---------------------------------------------------------------- allocation-free GEMM */
+/* No counterpart in the reference. mfb_sgemm without any device allocation, for callers
+ * that cannot allocate device memory when they call: code under a framework that owns
+ * the device-memory budget, latency-critical paths where cudaMalloc/cudaFree (which
+ * synchronize the device) or an out-of-memory failure mid-call are not acceptable, and
+ * plugins that may not touch their host process's allocator. Same arguments and results
+ * as mfb_sgemm (always the tcgen05 path, strict FP32 or TF32). The operand scratch is a
+ * static device array of MFB_NOALLOC_SCRATCH_BYTES (64 MiB, e.g. a 2048^3 strict GEMM)
+ * that every GPU loading the library holds until exit; larger problems return
+ * MFB_EINVAL. The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress); make it before any stream capture. All calls share the array:
+ * calls that overlap on the GPU race, so order them on one stream. */
+#define MFB_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+MFB_API mfb_status_t mfb_sgemm_noalloc(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
+                                       const float* b, float* c, const float* bias);
+
 /* ---------------------------------------------------------------- plans */
 typedef struct mfb_plan* mfb_plan_t;
 

@@ -4,3 +4,4 @@
 #include "gemm_tc.cu"
 #include "gemv.cu"
 #include "conv.cu"
+#include "noalloc.cu"
