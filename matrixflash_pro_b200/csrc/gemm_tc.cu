@@ -5,9 +5,11 @@
 // src/ops/gemm/plan/implementation.inc:111-151.
 #include "gemm_tc.cuh"
 #include "mfb_internal.h"
+#include "tc_pair_kernel.cuh"
 
 #include <algorithm>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 namespace mfb {
@@ -157,6 +159,7 @@ struct TcEntry {
     const void* fn;
     int smem;
     int threads;
+    int pair;  // SM-pair kernel (cluster of 2, 256-row tiles)
 };
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
@@ -164,11 +167,22 @@ TcEntry make_entry() {
     using P = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>;
     using L = TcLayout<P>;
     return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes,
-                   L::kThreads};
+                   L::kThreads, 0};
+}
+
+template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
+TcEntry make_pair_entry() {
+    using P = GemmPairProblem<BN, STAGES, PLANES, A_MN, B_MN>;
+    using L = TcPairLayout<P>;
+    return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_pair_kernel<P>), L::kBytes,
+                   L::kThreads, 1};
 }
 
 const TcEntry* kernel_table(int* count) {
     static const TcEntry table[] = {
+        // SM pairs, 256 x 256 tiles: strict and TF32
+        make_pair_entry<256, 3, 2, 0, 1>(),
+        make_pair_entry<256, 6, 1, 0, 1>(),
         // strict FP32 (3xTF32 split planes, chunked round-to-nearest accumulation)
         make_entry<256, 2, 2, 0, 1>(),
         make_entry<128, 3, 2, 0, 1>(),
@@ -193,7 +207,7 @@ const TcEntry* find_kernel(const TcConfig& c) {
     const TcEntry* t = kernel_table(&count);
     for (int i = 0; i < count; ++i)
         if (t[i].bn == c.bn && t[i].stages == c.stages && t[i].planes == c.planes && t[i].a_mn == c.a_mn &&
-            t[i].b_mn == c.b_mn)
+            t[i].b_mn == c.b_mn && t[i].pair == c.pair)
             return &t[i];
     return nullptr;
 }
@@ -243,11 +257,15 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
     int n_ok = 0;
     for (int i = 0; i < count && n_ok < 16; ++i)
         if (t[i].planes == planes && t[i].a_mn == a_mn && t[i].b_mn == b_mn) order[n_ok++] = i;
+    // SM pairs first when they fill the GPU (their 256-row tiles halve B's shared-memory
+    // traffic per FLOP), then the widest single-CTA tile that fills it, then narrower ones.
     std::sort(order, order + n_ok, [&](int x, int y) {
         auto score = [&](int idx) {
-            const long long tiles = tiles_m * ((d.n + t[idx].bn - 1) / t[idx].bn);
-            const bool fills = tiles >= (sms * 4) / 5;
-            return (fills ? 1000 : 0) + (fills ? t[idx].bn : -t[idx].bn);
+            const long long rows = t[idx].pair ? (d.m + 2 * kTcBM - 1) / (2 * kTcBM) : tiles_m;
+            const long long tiles = rows * ((d.n + t[idx].bn - 1) / t[idx].bn);
+            const long long slots = t[idx].pair ? sms / 2 : sms;
+            const bool fills = tiles >= (slots * 4) / 5;
+            return (fills ? 1000 : 0) + (fills && t[idx].pair ? 500 : 0) + (fills ? t[idx].bn : -t[idx].bn);
         };
         return score(x) > score(y);
     });
@@ -259,6 +277,7 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
         c.planes = planes;
         c.a_mn = a_mn;
         c.b_mn = b_mn;
+        c.pair = t[order[i]].pair;
         out[n_out++] = c;
     }
     return n_out;
@@ -342,7 +361,8 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     p.n = d.n;
     p.k = d.k;
     p.num_kb = (d.k + kBK - 1) / kBK;
-    p.tiles_m = (d.m + kTcBM - 1) / kTcBM;
+    const int tile_rows = cfg.pair ? 2 * kTcBM : kTcBM;
+    p.tiles_m = (d.m + tile_rows - 1) / tile_rows;
     p.tiles_n = (d.n + cfg.bn - 1) / cfg.bn;
     p.group_m = 16;
     p.c = c;
@@ -360,17 +380,55 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     cudaGetDevice(&dev);
     // Persistent: one CTA per SM, or fewer when the caller leaves SMs to a concurrent collective.
     const int sms = sm_limit > 0 ? std::min(sm_limit, sm_count(dev)) : sm_count(dev);
-    const long long grid = std::min<long long>(tiles, sms);
     static std::mutex attr_mutex;
     {
         std::lock_guard<std::mutex> lock(attr_mutex);
         MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem),
                      "cudaFuncSetAttribute(max dynamic smem)");
+        if (e->pair)
+            MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 0),
+                         "cudaFuncSetAttribute(cluster size)");
     }
     void* args[] = {&map_a, &map_b, &p};
-    MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(e->threads), args,
-                                  static_cast<size_t>(e->smem), stream),
-                 "tcgen05 GEMM launch");
+    if (!e->pair) {
+        const long long grid = std::min<long long>(tiles, sms);
+        MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(e->threads), args,
+                                      static_cast<size_t>(e->smem), stream),
+                     "tcgen05 GEMM launch");
+        return MFB_OK;
+    }
+    // SM pairs: clusters of 2 CTAs, as many as can be co-resident (capped by the SM limit).
+    cudaLaunchConfig_t lc{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.blockDim = dim3(e->threads);
+    lc.dynamicSmemBytes = static_cast<size_t>(e->smem);
+    lc.stream = stream;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    // Co-resident clusters per (device, kernel), queried once.
+    static std::mutex cluster_mutex;
+    static std::map<std::pair<int, const void*>, int> cluster_cache;
+    int max_clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(cluster_mutex);
+        auto it = cluster_cache.find({dev, e->fn});
+        if (it != cluster_cache.end()) max_clusters = it->second;
+    }
+    if (max_clusters == 0) {
+        lc.gridDim = dim3(static_cast<unsigned>(2 * (sm_count(dev) / 2)));
+        MFB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, e->fn, &lc), "cudaOccupancyMaxActiveClusters");
+        if (max_clusters <= 0) return fail(MFB_EUNSUPPORTED, "no SM pair can host the pair GEMM kernel");
+        std::lock_guard<std::mutex> lock(cluster_mutex);
+        cluster_cache[{dev, e->fn}] = max_clusters;
+    }
+    const long long pairs = std::min<long long>({tiles, static_cast<long long>(max_clusters),
+                                                 static_cast<long long>(std::max(1, sms / 2))});
+    lc.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    MFB_CUDA_TRY(cudaLaunchKernelExC(&lc, e->fn, args), "tcgen05 pair GEMM launch");
     return MFB_OK;
 }
 

@@ -61,6 +61,7 @@ struct TcConfig {
     int planes = 2;   // 2 = strict 3xTF32, 1 = TF32
     int a_mn = 0;     // A stored transposed (MN-major)
     int b_mn = 1;     // B stored untransposed (MN-major)
+    int pair = 0;     // 1: SM-pair kernel (cta_group::2, 256 x bn tiles)
 };
 
 // Admissible tile configurations for a problem, best-guess first.
