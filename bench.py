@@ -210,13 +210,166 @@ def run_reference_arm(args, wl):
     return 0
 
 
+AUX_WORKLOADS = {
+    # GEMV / skinny GEMM: A 16384 x 16384 ~ U[-1,1], x 16384 x n ~ N(0,1), alpha 1, beta 0.
+    "gemv_n1": ("gemv", 1), "gemv_n4": ("gemv", 4), "gemv_n16": ("gemv", 16),
+    # conv2d forward, stride 1, pad 1, 3x3: (N, C, H, W, K); x ~ U[-1,1], w ~ N(0, 2/fan_in), bias 0.
+    "conv_c4a": ("conv", (8, 3, 32, 32, 16)), "conv_c4b": ("conv", (256, 64, 56, 56, 64)),
+}
+
+
+def run_aux_workload(args):
+    """GEMV and conv2d workloads: one GPU per process (N > 1 runs independent replicas)."""
+    import torch
+    import matrixflash_pro_b200 as mf
+    import oracle
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    torch.cuda.set_device(local)
+    kind, shape = AUX_WORKLOADS[args.workload]
+    gen = torch.Generator(device="cuda").manual_seed(20261001 + rank)
+    peaks, peak_src = read_peaks()
+    strict = args.precision == "fp32"
+    prec = mf.GemmPrecision.fp32 if strict else mf.GemmPrecision.tf32
+    if kind == "gemv":
+        n = shape
+        m = k = 16384
+        A = torch.rand((m, k), device="cuda", generator=gen) * 2 - 1
+        X = torch.randn((k, n), device="cuda", generator=gen)
+        Y = torch.empty((m, n), device="cuda")
+        work = 4.0 * (m * k + k * n + m * n)  # algorithmic bytes per step
+        unit, metric_unit = "GB/s", 1e9
+        desc = f"GEMV/skinny GEMM A 16384x16384 x B 16384x{n}, alpha 1, beta 0 (A alone is 1 GiB > L2)"
+
+        def step():
+            mf.gemv(A, X, Y)
+
+        host = [torch.empty_like(A, device="cpu").pin_memory(), torch.empty_like(X, device="cpu").pin_memory()]
+        host[0].copy_(A)
+        host[1].copy_(X)
+        y_host = torch.empty_like(Y, device="cpu").pin_memory()
+
+        def e2e_step():
+            A.copy_(host[0], non_blocking=True)
+            X.copy_(host[1], non_blocking=True)
+            step()
+            y_host.copy_(Y, non_blocking=True)
+
+        h2d, d2h = (A.numel() + X.numel()) * 4, Y.numel() * 4
+        roof = {"bound": "hbm", "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "peak_basis": f"hbm_gbs of {peak_src} MEASURED_PEAKS.json", "kernel": f"gemv_rows_kernel (n={n})"}
+        launches = 1
+
+        def cpu_sample():
+            rows = 2048
+            a = A[:rows].cpu().numpy()
+            x = X.cpu().numpy()
+            c = np.zeros((rows, n), np.float32)
+            impl = "reference" if oracle.reference_available() else "restatement"
+            oracle.gemm_f32(rows, n, k, a, k, x, n, c, n, 1.0, 0.0, impl=impl)
+            t0 = time.perf_counter()
+            for _ in range(3):
+                oracle.gemm_f32(rows, n, k, a, k, x, n, c, n, 1.0, 0.0, impl=impl)
+            dt = (time.perf_counter() - t0) / 3
+            info = oracle.reference_info() if impl == "reference" else {"worker_count": 1}
+            return {"value": 4.0 * (rows * k + k * n + rows * n) / dt / 1e9, "unit": "GB/s",
+                    "cores": info["worker_count"], "kind": "reference" if impl == "reference" else "port",
+                    "sample": f"{rows} of the 16384 rows, full k and n, gemm_f32, mean of 3"}
+    else:
+        nb, c, h, w, kf = shape
+        x = torch.rand((nb, c, h, w), device="cuda", generator=gen) * 2 - 1
+        wt = torch.randn((kf, c, 3, 3), device="cuda", generator=gen) * float(np.sqrt(2.0 / (c * 9)))
+        bias = torch.zeros(kf, device="cuda")
+        y = torch.empty((nb, kf, h, w), device="cuda")
+        work = 2.0 * nb * kf * h * w * c * 9  # algorithmic FLOPs per step
+        unit, metric_unit = "TFLOPS", 1e12
+        desc = f"conv2d forward NCHW {nb}x{c}x{h}x{w}, {kf} 3x3 filters, stride 1, pad 1"
+
+        def step():
+            mf.conv2d_into(x, wt, bias, y, 1, 1, prec)
+
+        x_h = torch.empty_like(x, device="cpu").pin_memory()
+        x_h.copy_(x)
+        y_h = torch.empty_like(y, device="cpu").pin_memory()
+
+        def e2e_step():
+            x.copy_(x_h, non_blocking=True)
+            step()
+            y_h.copy_(y, non_blocking=True)
+
+        h2d, d2h = x.numel() * 4, y.numel() * 4
+        passes = 6.0 if strict else 2.0
+        roof = {"bound": "tensor", "peak": peaks["bf16_tflops"] / passes, "unit": "TFLOP/s",
+                "peak_basis": f"bf16_tflops/{int(passes)} of {peak_src} MEASURED_PEAKS.json",
+                "kernel": "tc_persistent_kernel<ConvProblem> (implicit GEMM; time includes the layout prepass)"}
+        launches = 3
+
+        def cpu_sample():
+            xs = x[:1].cpu().numpy()
+            ws = wt.cpu().numpy()
+            bs = bias.cpu().numpy()
+            t0 = time.perf_counter()
+            oracle.conv2d_f32(xs, ws, bs, 1, 1)
+            dt = time.perf_counter() - t0
+            return {"value": 2.0 * kf * h * w * c * 9 / dt / 1e12, "unit": "TFLOPS", "cores": 1, "kind": "port",
+                    "sample": "1 image, single-thread restatement of conv2d_kernel (the reference has no CPU conv)"}
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    mf.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    mf.sync()
+    value = work * args.steps / (ms / 1e3) / metric_unit
+    roof.update({"achieved": value, "frac": value / roof["peak"], "traffic": read_profile_traffic(
+        f"{args.workload}_{args.precision}" if kind == "conv" else args.workload)})
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e_step()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        s1.record()
+        torch.cuda.synchronize()
+        e2e = {"value": work * args.e2e_steps / (s0.elapsed_time(s1) / 1e3) / metric_unit, "unit": unit,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_sample()
+        except Exception as exc:
+            cpu = {"value": None, "unit": unit, "cores": None, "kind": None, "sample": f"failed: {exc}"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value * world, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": desc, "precision": args.precision, "parallelism": f"{world} independent replicas",
+                       "l2": "inputs larger than L2 every step"},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches * args.steps,
+            "clocks": clocks.summary()}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mfb", "reference"], default="mfb")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="linear")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(AUX_WORKLOADS), default="linear")
     ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -224,6 +377,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload in AUX_WORKLOADS:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is defined for the GEMM "
+                              "workloads (the reference's CPU path for this path is gemm_f32)"}))
+            return 0
+        return run_aux_workload(args)
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference_arm(args, wl)
