@@ -153,8 +153,9 @@ MFB_API mfb_status_t mfb_plan_execute(mfb_plan_t plan, mfb_stream_t stream, cons
 /* The two phases of mfb_plan_execute, for callers that reuse prepared operands or
  * time the phases: prepare runs the operand prepass (3xTF32 hi/lo split, or TF32
  * round-to-nearest) into the plan's scratch; multiply runs only the GEMM kernel on the
- * prepared operands (a/b are still passed; GEMV plans read them there). No reference
- * counterpart: GemmPlan::execute (gemm.hpp:47) is both phases in one call. */
+ * prepared operands (a/b are still passed; GEMV plans read them there). prepare with
+ * a NULL operand skips that operand, so A can be prepared while B is still arriving. No
+ * reference counterpart: GemmPlan::execute (gemm.hpp:47) is both phases in one call. */
 MFB_API mfb_status_t mfb_plan_prepare(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b);
 MFB_API mfb_status_t mfb_plan_multiply(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
                                        float* c, float alpha, float beta, const float* bias);

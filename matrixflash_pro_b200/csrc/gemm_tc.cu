@@ -313,7 +313,8 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     const bool run_prepass = (phases & kPhasePrepare) != 0;
     const bool run_gemm = (phases & kPhaseMultiply) != 0;
 
-    // --- operand preparation: split planes (strict) or repack (TF32, unaligned) ---
+    // --- operand preparation: hi/lo planes (strict) or one rounded plane (TF32). In the
+    // prepare-only phase a null operand pointer skips that operand. ---
     PreparedOperand ops[2];
     size_t used = 0;
     char* ws = static_cast<char*>(workspace);
@@ -332,7 +333,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         used += need;
         const long long total_groups = static_cast<long long>(op.rows) * (ldp / 4);
         const int blocks = static_cast<int>(std::min<long long>((total_groups + 255) / 256, 148LL * 8));
-        if (run_prepass && blocks > 0) {
+        if (run_prepass && blocks > 0 && src != nullptr) {
             split_tf32_kernel<<<blocks, 256, 0, stream>>>(src, ld, op.rows, op.cols, hi, lo, ldp,
                                                          (ld % 4 == 0 && aligned16(src)) ? 1 : 0);
             MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");

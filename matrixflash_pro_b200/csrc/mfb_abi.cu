@@ -214,8 +214,8 @@ mfb_status_t plan_run(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, co
     const bool multiply = (phases & kPhaseMultiply) != 0;
     if (multiply) {
         MFB_TRY(validate_desc(&d, a, b, c, bias, true));
-    } else if (d.m > 0 && d.n > 0 && d.k > 0 && (!a || !b)) {
-        return fail(MFB_EINVAL, "null A or B pointer");
+    } else if (d.m > 0 && d.n > 0 && d.k > 0 && !a && !b) {
+        return fail(MFB_EINVAL, "mfb_plan_prepare needs A, B or both");
     }
     DeviceGuard guard;
     MFB_TRY(select_device(plan->device));

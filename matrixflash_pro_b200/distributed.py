@@ -68,14 +68,19 @@ def schedule(k: int, world: int, beta: float, comm_sms: int, total_sms: int) -> 
 
 
 def run_schedule(sched: PanelSchedule, b_rows: Callable[[int, int], torch.Tensor], panel_gemm: PanelGemm,
-                 group=None, src: int = 0) -> None:
-    """Issues the broadcasts (async, NCCL stream) then the per-panel GEMMs (current stream).
-    `b_rows(k0, k1)` returns the contiguous row block of B's storage for a panel."""
+                 group=None, src: int = 0,
+                 before_wait: Optional[Callable[[int, Tuple[int, int]], None]] = None) -> None:
+    """Issues the broadcasts (async, NCCL stream), then `before_wait(i, panel)` for every
+    panel (work that does not read B, e.g. preparing A), then the per-panel GEMMs (current
+    stream). `b_rows(k0, k1)` returns the contiguous row block of B's storage for a panel."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     works = []
     if world > 1:
         for (k0, k1) in sched.panels:
             works.append(dist.broadcast(b_rows(k0, k1), src=src, group=group, async_op=True))
+    if before_wait is not None:
+        for i, panel in enumerate(sched.panels):
+            before_wait(i, panel)
     for i, panel in enumerate(sched.panels):
         if works:
             works[i].wait()  # current stream waits for this panel's broadcast only
@@ -144,12 +149,16 @@ class RowSplitGemm:
         sched = PanelSchedule(self.sched.panels, [beta] + [1.0] * (len(self.sched.panels) - 1), self.sched.sm_limits)
         self.kernel_events = []
 
+        def prepare_a(i, panel):
+            # A's split/rounding prepass does not read B: it runs while B is in flight.
+            self.plans[i].prepare(stream, a0 + 4 * panel[0], 0)
+
         def panel_gemm(i, panel, pbeta, sm_limit):
             k0, _ = panel
             plan = self.plans[i]
             a_ptr = a0 + 4 * k0
             b_ptr = b0 + 4 * k0 * self.ldb
-            plan.prepare(stream, a_ptr, b_ptr)
+            plan.prepare(stream, 0, b_ptr)
             plan.set_sm_limit(sm_limit)
             if time_kernels:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -162,14 +171,12 @@ class RowSplitGemm:
         def b_rows(k0, k1):
             return B.as_strided((k1 - k0, self.ldb), (self.ldb, 1), B.storage_offset() + k0 * self.ldb)
 
-        run_schedule(sched, b_rows, panel_gemm, self.group, self.src)
+        run_schedule(sched, b_rows, panel_gemm, self.group, self.src, before_wait=prepare_a)
 
     def launches_per_step(self) -> int:
-        """Kernels of this library per step: prepass split of A and B + GEMM, per panel."""
-        return (3 if self._strict() else 1) * len(self.plans)
-
-    def _strict(self) -> bool:
-        return self.plans[0].desc.precision == int(GemmPrecision.fp32)
+        """Kernels of this library per step: the prepass of A (hi/lo split, or TF32 rounding),
+        the prepass of B and the GEMM, per panel."""
+        return 3 * len(self.plans)
 
     def kernel_ms(self) -> float:
         return sum(e0.elapsed_time(e1) for (e0, e1) in self.kernel_events)

@@ -292,3 +292,28 @@ def test_plan_info_and_no_tcgen05_for_vectors():
     t = mf.GemmPlan(4096, 4096, 64, mf.GemmOptions(precision=TF32))
     assert t.info().kernel.decode() == "tcgen05_tf32"
     assert t.info().workspace_bytes >= (4096 * 64 + 64 * 4096) * 4  # one rounded TF32 plane per operand
+
+
+@pytest.mark.parametrize("precision", [FP32, TF32])
+def test_prepare_operands_one_at_a_time(precision):
+    """mfb_plan_prepare with a NULL operand prepares only the other one (A before B, as the
+    row split does while B is still arriving); the multiply then equals mfb_plan_execute."""
+    from matrixflash_pro_b200 import _lib
+    from matrixflash_pro_b200.gemm import _stream_handle
+    m, n, k = 300, 520, 700
+    g = torch.Generator(device="cuda").manual_seed(9)
+    A = torch.randn((m, k), device="cuda", generator=g)
+    B = torch.randn((k, n), device="cuda", generator=g)
+    C0 = torch.randn((m, n), device="cuda", generator=g)
+    p = mf.GemmPlan(m, n, k, mf.GemmOptions(precision=precision))
+    want = C0.clone()
+    p.execute(A, B, want, 0.5, 1.0)
+    got = C0.clone()
+    lib, h, s = _lib.lib(), p._handle, _stream_handle()
+    _lib.check(lib.mfb_plan_prepare(h, s, A.data_ptr(), 0), "prepare A")
+    _lib.check(lib.mfb_plan_prepare(h, s, 0, B.data_ptr()), "prepare B")
+    _lib.check(lib.mfb_plan_multiply(h, s, A.data_ptr(), B.data_ptr(), got.data_ptr(), 0.5, 1.0, 0), "multiply")
+    mf.sync()
+    assert torch.equal(got, want)
+    with pytest.raises(mf.InvalidArgumentError):
+        _lib.check(lib.mfb_plan_prepare(h, s, 0, 0), "prepare nothing")
