@@ -212,7 +212,7 @@ def run_reference_arm(args, wl):
 
 AUX_WORKLOADS = {
     # GEMV / skinny GEMM: A 16384 x 16384 ~ U[-1,1], x 16384 x n ~ N(0,1), alpha 1, beta 0.
-    "gemv_n1": ("gemv", 1), "gemv_n4": ("gemv", 4), "gemv_n16": ("gemv", 16),
+    "gemv_n1": ("gemv", 1), "gemv_n4": ("gemv", 4), "gemv_n8": ("gemv", 8), "gemv_n16": ("gemv", 16),
     # conv2d forward, stride 1, pad 1, 3x3: (N, C, H, W, K); x ~ U[-1,1], w ~ N(0, 2/fan_in), bias 0.
     "conv_c4a": ("conv", (8, 3, 32, 32, 16)), "conv_c4b": ("conv", (256, 64, 56, 56, 64)),
 }
@@ -259,7 +259,9 @@ def run_aux_workload(args):
 
         h2d, d2h = (A.numel() + X.numel()) * 4, Y.numel() * 4
         roof = {"bound": "hbm", "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "peak_basis": f"hbm_gbs of {peak_src} MEASURED_PEAKS.json", "kernel": f"gemv_rows_kernel (n={n})"}
+                "peak_basis": f"hbm_gbs of {peak_src} MEASURED_PEAKS.json",
+                "kernel": f"gemv_tile_kernel (TMA-fed, {1 if n == 1 else 4 if n <= 4 else 8 if n <= 8 else 16}-column "
+                          f"variant, n={n})"}
         launches = 1
 
         def cpu_sample():

@@ -50,6 +50,53 @@ def test_gemv_widths_and_strides(n):
                   np.abs(a).max(), np.abs(b).max())
 
 
+# 16-byte aligned operands with lda, ldb multiples of 4 (or a contiguous x for n = 1) take
+# the TMA tile kernel. The shapes cover the 1-, 4-, 8- and 16-column variants, each
+# rows-per-lane instance (tile rows <= 32, <= 64, <= 112, <= 128), CTAs that own two
+# tiles (m = 20000), k not a multiple of the 128-k stage, and a k shorter than one stage.
+@pytest.mark.parametrize("m,n,k,ldb", [(1003, 5, 1537, 12), (300, 8, 5000, 12), (6000, 9, 700, 16),
+                                       (16000, 16, 300, 20), (20000, 12, 513, 16), (17000, 16, 129, 16),
+                                       (2000, 16, 40, 16), (5000, 1, 777, 1), (20000, 1, 1000, 1),
+                                       (3000, 1, 600, 4), (9000, 3, 1100, 4), (16384, 4, 2000, 8)])
+def test_gemv_tile_kernel_shapes(m, n, k, ldb):
+    lda, ldc = (k + 3) // 4 * 4 + 4, n + 3
+    a = oracle.seeded(m * lda, seed=m + n)
+    b = oracle.seeded(k * ldb, "normal", seed=k)
+    c0 = oracle.seeded(m * ldc, "normal", seed=n)
+    A = to_dev(a.reshape(m, lda))[:, :k]
+    B = to_dev(b.reshape(k, ldb))[:, :n]
+    C = to_dev(c0.reshape(m, ldc).copy())
+    assert A.data_ptr() % 16 == 0 and B.data_ptr() % 16 == 0
+    mf.gemv(A, B, C[:, :n], 0.75, -0.5)
+    mf.sync()
+    got = C.cpu().numpy()
+    ref = c0.copy()
+    oracle.gemm_f32(m, n, k, a, lda, b, ldb, ref, ldc, 0.75, -0.5)
+    ref = ref.reshape(m, ldc)
+    assert np.array_equal(got[:, n:], ref[:, n:]), "columns beyond n were written"
+    assert_strict(got[:, :n], ref[:, :n], oracle.gemm_f64(m, n, k, a, lda, b, ldb, c0, ldc, 0.75, -0.5), k,
+                  np.abs(a).max(), np.abs(b).max(), f"{m}x{n}x{k}")
+
+
+def test_gemv_tile_kernel_bias_epilogues():
+    """bias + ReLU / GELU through a plan whose path is the tile kernel (n = 12)."""
+    m, n, k = 5000, 12, 1000
+    a = oracle.seeded(m * k, seed=1)
+    b = oracle.seeded(k * n, "normal", seed=2)
+    bias = oracle.seeded(n, "normal", seed=3)
+    for ep in (mf.GemmEpilogue.bias_relu, mf.GemmEpilogue.bias_gelu):
+        C = torch.empty((m, n), device="cuda")
+        mf.sgemm(to_dev(a.reshape(m, k)), to_dev(b.reshape(k, n)), C, 1.0, 0.0, mf.GemmOptions(epilogue=ep),
+                 to_dev(bias))
+        mf.sync()
+        ref = np.zeros(m * n, np.float32)
+        oracle.gemm_f32(m, n, k, a, k, b, n, ref, n)
+        oracle.epilogue_f32(ref, n, bias, m, n, int(ep) - 1)  # oracle modes: 0 bias, 1 +ReLU, 2 +GELU
+        err = np.abs(C.cpu().numpy() - ref.reshape(m, n)).max()
+        # ReLU is 1-Lipschitz and tanh-GELU at most 1.13: the GEMM bound carries over.
+        assert err <= 1.13 * oracle.elementwise_bound(k, np.abs(a).max(), np.abs(b).max()), (ep, err)
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("n", [1, 4, 16])
 def test_gemv_full_size_sampled_rows(n):
