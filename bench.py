@@ -215,6 +215,8 @@ AUX_WORKLOADS = {
     "gemv_n1": ("gemv", 1), "gemv_n4": ("gemv", 4), "gemv_n8": ("gemv", 8), "gemv_n16": ("gemv", 16),
     # conv2d forward, stride 1, pad 1, 3x3: (N, C, H, W, K); x ~ U[-1,1], w ~ N(0, 2/fan_in), bias 0.
     "conv_c4a": ("conv", (8, 3, 32, 32, 16)), "conv_c4b": ("conv", (256, 64, 56, 56, 64)),
+    # strided-batched GEMM (batch_matmul): (batch, m, n, k); A, B ~ U[-1,1], alpha 1, beta 0.
+    "bmm_b16_2048": ("bmm", (16, 2048, 2048, 2048)),
 }
 
 
@@ -279,6 +281,51 @@ def run_aux_workload(args):
             return {"value": 4.0 * (rows * k + k * n + rows * n) / dt / 1e9, "unit": "GB/s",
                     "cores": info["worker_count"], "kind": "reference" if impl == "reference" else "port",
                     "sample": f"{rows} of the 16384 rows, full k and n, gemm_f32, mean of 3"}
+    elif kind == "bmm":
+        nb, m, n, k = shape
+        A = torch.rand((nb, m, k), device="cuda", generator=gen) * 2 - 1
+        B = torch.rand((nb, k, n), device="cuda", generator=gen) * 2 - 1
+        C = torch.empty((nb, m, n), device="cuda")
+        work = 2.0 * nb * m * n * k
+        unit, metric_unit = "TFLOPS", 1e12
+        desc = f"strided-batched GEMM {nb} x ({m}x{k} @ {k}x{n}), alpha 1, beta 0 (operands 3 x {nb * m * k * 4 >> 20} MiB)"
+        opts = mf.GemmOptions(precision=prec)
+
+        def step():
+            mf.sgemm_strided_batched(A, B, C, 1.0, 0.0, opts)
+
+        host = [torch.empty_like(A, device="cpu").pin_memory(), torch.empty_like(B, device="cpu").pin_memory()]
+        host[0].copy_(A)
+        host[1].copy_(B)
+        c_host = torch.empty_like(C, device="cpu").pin_memory()
+
+        def e2e_step():
+            A.copy_(host[0], non_blocking=True)
+            B.copy_(host[1], non_blocking=True)
+            step()
+            c_host.copy_(C, non_blocking=True)
+
+        h2d, d2h = (A.numel() + B.numel()) * 4, C.numel() * 4
+        passes = 6.0 if strict else 2.0
+        roof = {"bound": "tensor", "peak": peaks["bf16_tflops"] / passes, "unit": "TFLOP/s",
+                "peak_basis": f"bf16_tflops/{int(passes)} of {peak_src} MEASURED_PEAKS.json",
+                "kernel": "tc_persistent_kernel<GemmProblem> over the batch (time includes the split prepass)"}
+        launches = 3
+
+        def cpu_sample():
+            rows = 256
+            a = A[0, :rows].cpu().numpy()
+            b = B[0].cpu().numpy()
+            c = np.zeros((rows, n), np.float32)
+            impl = "reference" if oracle.reference_available() else "restatement"
+            oracle.gemm_f32(rows, n, k, a, k, b, n, c, n, 1.0, 0.0, impl=impl)
+            t0 = time.perf_counter()
+            oracle.gemm_f32(rows, n, k, a, k, b, n, c, n, 1.0, 0.0, impl=impl)
+            dt = time.perf_counter() - t0
+            info = oracle.reference_info() if impl == "reference" else {"worker_count": 1}
+            return {"value": 2.0 * rows * n * k / dt / 1e12, "unit": "TFLOPS", "cores": info["worker_count"],
+                    "kind": "reference" if impl == "reference" else "port",
+                    "sample": f"{rows} rows of batch entry 0, gemm_f32 (the reference batches through cuBLAS only)"}
     else:
         nb, c, h, w, kf = shape
         x = torch.rand((nb, c, h, w), device="cuda", generator=gen) * 2 - 1

@@ -12,6 +12,8 @@
  *                                   (body: src/hw/cuda_backend.cu:91-99,159-163)
  *   mfb_sgemm                       the cublasLtMatmul/cublasGemmEx call of GemmPlan::Impl::run_ptr
  *                                   src/ops/gemm/plan/implementation.inc:128-151
+ *   mfb_sgemm_strided_batched       cublasSgemmStridedBatched in batch_matmul and its backward
+ *                                   src/nn/batch.cu:12-35, src/nn/backward/batched_matmul.inc:7-55
  *   mfb_plan_*                      GemmPlan ctor/execute/tune/rows/cols/inner/candidate_count
  *                                   include/matrix_pro/ops/gemm.hpp:36-62
  *                                   (src/ops/gemm/plan/implementation.inc:5-152, tuning.inc:5-66)
@@ -113,6 +115,19 @@ MFB_API mfb_status_t mfb_cuda_device_count(int* count);
  * (CUDA graph capture) create a plan. bias: n floats, required iff epilogue != NONE. */
 MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
                                const float* b, float* c, const float* bias);
+
+/* ---------------------------------------------------------------- strided-batched GEMM */
+/* batch_count GEMMs that share one descriptor: C_i = epilogue(alpha op(A_i) op(B_i) + beta C_i)
+ * with A_i = a + i*stride_a, B_i = b + i*stride_b, C_i = c + i*stride_c (strides in floats;
+ * a stride of 0 reuses one operand for every entry). Replaces cublasSgemmStridedBatched in
+ * batch_matmul (src/nn/batch.cu:12-35) and in its backward, batch_matmul_backward_left
+ * (G x B^T: trans_b) and batch_matmul_backward_right (A^T x G: trans_a)
+ * (src/nn/backward/batched_matmul.inc:7-55). All entries run in one tcgen05 launch; the
+ * outputs may not overlap each other or any input. batch_count <= 65535. */
+MFB_API mfb_status_t mfb_sgemm_strided_batched(int device, mfb_stream_t stream, const mfb_gemm_desc* desc,
+                                               const float* a, long long stride_a, const float* b,
+                                               long long stride_b, float* c, long long stride_c, int batch_count,
+                                               const float* bias);
 
 /* ---------------------------------------------------------------- allocation-free GEMM */
 /* No counterpart in the reference. mfb_sgemm without any device allocation, for callers

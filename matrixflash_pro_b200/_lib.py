@@ -19,7 +19,7 @@ MFB_OK, MFB_EINVAL, MFB_ECUDA, MFB_ETIMEOUT, MFB_ENCCL, MFB_EUNSUPPORTED, MFB_EN
 EXPORTED_SYMBOLS = (
     "mfb_status_string", "mfb_last_error", "mfb_version", "mfb_device_status", "mfb_set_wait_limit_ns",
     "mfb_get_wait_limit_ns", "mfb_sync", "mfb_cuda_gemm", "mfb_cuda_sync", "mfb_cuda_device_count", "mfb_sgemm",
-    "mfb_sgemm_noalloc",
+    "mfb_sgemm_noalloc", "mfb_sgemm_strided_batched",
     "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_set_sm_limit",
     "mfb_plan_tune", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
     "mfb_conv2d_fwd", "mfb_naive_sgemm", "mfb_probe_wait_timeout",
@@ -63,6 +63,8 @@ def _declare(lib):
         "mfb_cuda_device_count": (st, [ctypes.POINTER(ctypes.c_int)]),
         "mfb_sgemm": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_sgemm_noalloc": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
+        "mfb_sgemm_strided_batched": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, ctypes.c_longlong, _vp,
+                                           ctypes.c_longlong, _vp, ctypes.c_longlong, ctypes.c_int, _vp]),
         "mfb_plan_create": (st, [ctypes.c_int, ctypes.POINTER(GemmDesc), ctypes.POINTER(_vp)]),
         "mfb_plan_execute": (st, [_vp, _vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_float, _vp]),
         "mfb_plan_prepare": (st, [_vp, _vp, _vp, _vp]),

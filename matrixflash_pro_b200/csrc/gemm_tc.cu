@@ -28,8 +28,14 @@ __device__ __forceinline__ float round_tf32(float x) {
 // hi + lo carries 22 significant bits of x. lo == nullptr writes only hi: the TF32
 // mode's operands, rounded to nearest like cuBLAS/CUTLASS TF32 conversion (the tensor
 // core itself would truncate the low 13 bits, a bias that shows on same-sign data).
+// blockIdx.y walks a strided batch: source matrix y at x + y * x_batch, its planes at
+// hi/lo + y * p_batch.
 __global__ void split_tf32_kernel(const float* __restrict__ x, long long ldx, int rows, int cols,
-                                  float* __restrict__ hi, float* __restrict__ lo, long long ldp, int vec_in) {
+                                  float* __restrict__ hi, float* __restrict__ lo, long long ldp, int vec_in,
+                                  long long x_batch, long long p_batch) {
+    x += blockIdx.y * x_batch;
+    hi += blockIdx.y * p_batch;
+    if (lo != nullptr) lo += blockIdx.y * p_batch;
     const long long groups_per_row = ldp / 4;
     const long long total = static_cast<long long>(rows) * groups_per_row;
     for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
@@ -100,21 +106,36 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 3-D map over a stored row-major matrix (cols contiguous) with an outer plane axis.
-// K-major tiles use the 128B swizzle with 16-byte atoms; MN-major TF32 tiles the 128B
-// swizzle with 32-byte atoms, the only shared-memory layout tcgen05 accepts for them.
+// Map over a stored row-major matrix (cols contiguous) with an outer plane axis: 3-D
+// (cols, rows, plane) for the SM-pair kernels, 4-D (cols, rows, batch, plane) for the
+// single-CTA kernels. K-major tiles use the 128B swizzle with 16-byte atoms; MN-major
+// TF32 tiles the 128B swizzle with 32-byte atoms, the only shared-memory layout tcgen05
+// accepts for them.
 mfb_status_t encode_operand(CUtensorMap* map, const float* base, int rows, int cols, long long ld, int planes,
-                            long long plane_stride_floats, int box_cols, int box_rows, bool mn_major) {
+                            long long plane_stride_floats, int box_cols, int box_rows, bool mn_major, bool batched,
+                            int batch = 1, long long batch_stride_floats = 0) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail(MFB_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
-                                static_cast<cuuint64_t>(planes)};
-    long long plane_stride = plane_stride_floats > 0 ? plane_stride_floats : ld * static_cast<long long>(rows);
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(plane_stride) * 4};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows),
-                               static_cast<cuuint32_t>(planes)};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+    const long long plane_stride = plane_stride_floats > 0 ? plane_stride_floats : ld * static_cast<long long>(rows);
+    const long long batch_stride = batch_stride_floats > 0 ? batch_stride_floats : ld * static_cast<long long>(rows);
+    const int rank = batched ? 4 : 3;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), 0, 0};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld) * 4, 0, 0};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1, 1};
+    if (batched) {
+        dims[2] = static_cast<cuuint64_t>(batch);
+        dims[3] = static_cast<cuuint64_t>(planes);
+        strides[1] = static_cast<cuuint64_t>(batch_stride) * 4;
+        strides[2] = static_cast<cuuint64_t>(plane_stride) * 4;
+        box[3] = static_cast<cuuint32_t>(planes);
+    } else {
+        dims[2] = static_cast<cuuint64_t>(planes);
+        strides[1] = static_cast<cuuint64_t>(plane_stride) * 4;
+        box[2] = static_cast<cuuint32_t>(planes);
+    }
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<cuuint32_t>(rank), const_cast<float*>(base),
+                    dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE,
                     mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -219,6 +240,7 @@ struct PreparedOperand {
     int rows = 0, cols = 0;
     long long ld = 0;
     long long plane_stride = 0;  // floats; 0 when one plane
+    long long batch_stride = 0;  // floats between batch entries of one plane
     bool needs_prepass = false;
 };
 
@@ -244,7 +266,7 @@ size_t plane_floats(int rows, int cols) {
 // ------------------------------------------------------------------------------------
 // Configuration choice
 // ------------------------------------------------------------------------------------
-int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
+int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch) {
     const int planes = d.precision == MFB_PRECISION_TF32 ? 1 : 2;
     const int a_mn = d.trans_a ? 1 : 0;
     const int b_mn = d.trans_b ? 0 : 1;
@@ -256,13 +278,14 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
     int order[16];
     int n_ok = 0;
     for (int i = 0; i < count && n_ok < 16; ++i)
-        if (t[i].planes == planes && t[i].a_mn == a_mn && t[i].b_mn == b_mn) order[n_ok++] = i;
+        if (t[i].planes == planes && t[i].a_mn == a_mn && t[i].b_mn == b_mn && (batch == 1 || !t[i].pair))
+            order[n_ok++] = i;
     // SM pairs first when they fill the GPU (their 256-row tiles halve B's shared-memory
     // traffic per FLOP), then the widest single-CTA tile that fills it, then narrower ones.
     std::sort(order, order + n_ok, [&](int x, int y) {
         auto score = [&](int idx) {
             const long long rows = t[idx].pair ? (d.m + 2 * kTcBM - 1) / (2 * kTcBM) : tiles_m;
-            const long long tiles = rows * ((d.n + t[idx].bn - 1) / t[idx].bn);
+            const long long tiles = batch * rows * ((d.n + t[idx].bn - 1) / t[idx].bn);
             const long long slots = t[idx].pair ? sms / 2 : sms;
             const bool fills = tiles >= (slots * 4) / 5;
             return (fills ? 1000 : 0) + (fills && t[idx].pair ? 500 : 0) + (fills ? t[idx].bn : -t[idx].bn);
@@ -283,7 +306,7 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out) {
     return n_out;
 }
 
-size_t tc_workspace_bytes(const mfb_gemm_desc& d) {
+size_t tc_workspace_bytes(const mfb_gemm_desc& d, int batch) {
     size_t bytes = 0;
     for (int which = 0; which < 2; ++which) {
         int rows, cols;
@@ -291,7 +314,8 @@ size_t tc_workspace_bytes(const mfb_gemm_desc& d) {
         stored_dims(d, which == 0, &rows, &cols, &ld);
         (void)ld;
         // TF32: one round-to-nearest plane per operand; strict: hi and lo planes.
-        bytes += (d.precision == MFB_PRECISION_TF32 ? 1 : 2) * plane_floats(rows, cols) * 4;
+        bytes += (d.precision == MFB_PRECISION_TF32 ? 1 : 2) * plane_floats(rows, cols) * 4 *
+                 static_cast<size_t>(std::max(1, batch));
     }
     return bytes;
 }
@@ -307,14 +331,18 @@ mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c,
 
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
-                     int phases, int sm_limit) {
+                     int phases, int sm_limit, const TcBatch& batch) {
     const TcEntry* e = find_kernel(cfg);
     if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 kernel for this tile configuration");
+    const int nb = batch.count;
+    if (nb < 1 || nb > 65535) return fail(MFB_EINVAL, "batch count must be in [1, 65535]");
+    if (nb > 1 && e->pair) return fail(MFB_EUNSUPPORTED, "SM-pair kernels do not take a batch");
     const bool run_prepass = (phases & kPhasePrepare) != 0;
     const bool run_gemm = (phases & kPhaseMultiply) != 0;
 
-    // --- operand preparation: hi/lo planes (strict) or one rounded plane (TF32). In the
-    // prepare-only phase a null operand pointer skips that operand. ---
+    // --- operand preparation: hi/lo planes (strict) or one rounded plane (TF32), laid out
+    // [plane][batch entry][rows][cols rounded up to 4]. In the prepare-only phase a null
+    // operand pointer skips that operand. ---
     PreparedOperand ops[2];
     size_t used = 0;
     char* ws = static_cast<char*>(workspace);
@@ -323,24 +351,29 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         long long ld;
         stored_dims(d, which == 0, &op.rows, &op.cols, &ld);
         const float* src = which == 0 ? a : b;
+        const long long src_batch = which == 0 ? batch.stride_a : batch.stride_b;
         const long long ldp = round_up(op.cols, 4);
         const size_t pf = plane_floats(op.rows, op.cols);
-        const size_t need = pf * 4 * static_cast<size_t>(cfg.planes);
+        const size_t need = pf * 4 * static_cast<size_t>(cfg.planes) * static_cast<size_t>(nb);
         if (used + need > workspace_bytes || ws == nullptr)
             return fail(MFB_EINVAL, "workspace too small for the tcgen05 operand planes");
         float* hi = reinterpret_cast<float*>(ws + used);
-        float* lo = cfg.planes == 2 ? hi + pf : nullptr;
+        float* lo = cfg.planes == 2 ? hi + pf * nb : nullptr;
         used += need;
         const long long total_groups = static_cast<long long>(op.rows) * (ldp / 4);
-        const int blocks = static_cast<int>(std::min<long long>((total_groups + 255) / 256, 148LL * 8));
+        const int blocks = static_cast<int>(
+            std::min<long long>((total_groups + 255) / 256, std::max(1LL, 148LL * 8 / nb)));
+        const bool vec = ld % 4 == 0 && src_batch % 4 == 0 && aligned16(src);
         if (run_prepass && blocks > 0 && src != nullptr) {
-            split_tf32_kernel<<<blocks, 256, 0, stream>>>(src, ld, op.rows, op.cols, hi, lo, ldp,
-                                                         (ld % 4 == 0 && aligned16(src)) ? 1 : 0);
+            split_tf32_kernel<<<dim3(blocks, nb), 256, 0, stream>>>(src, ld, op.rows, op.cols, hi, lo, ldp,
+                                                                    vec ? 1 : 0, src_batch,
+                                                                    static_cast<long long>(pf));
             MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");
         }
         op.base = hi;
         op.ld = ldp;
-        op.plane_stride = cfg.planes == 2 ? static_cast<long long>(pf) : 0;
+        op.plane_stride = cfg.planes == 2 ? static_cast<long long>(pf) * nb : 0;
+        op.batch_stride = static_cast<long long>(pf);
         op.needs_prepass = true;
     }
     if (!run_gemm) return MFB_OK;
@@ -351,10 +384,10 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         const PreparedOperand& A = ops[0];
         // K-major A: box 32 (K) x 128 (M); MN-major A: box 32 (M) x 32 (K).
         MFB_TRY(encode_operand(&map_a, A.base, A.rows, A.cols, A.ld, cfg.planes, A.plane_stride, 32,
-                               cfg.a_mn ? 32 : kTcBM, cfg.a_mn != 0));
+                               cfg.a_mn ? 32 : kTcBM, cfg.a_mn != 0, !e->pair, nb, A.batch_stride));
         const PreparedOperand& B = ops[1];
         MFB_TRY(encode_operand(&map_b, B.base, B.rows, B.cols, B.ld, cfg.planes, B.plane_stride, 32,
-                               cfg.b_mn ? 32 : cfg.bn, cfg.b_mn != 0));
+                               cfg.b_mn ? 32 : cfg.bn, cfg.b_mn != 0, !e->pair, nb, B.batch_stride));
     }
 
     GemmTcParams p{};
@@ -365,6 +398,8 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     const int tile_rows = cfg.pair ? 2 * kTcBM : kTcBM;
     p.tiles_m = (d.m + tile_rows - 1) / tile_rows;
     p.tiles_n = (d.n + cfg.bn - 1) / cfg.bn;
+    p.batch = nb;
+    p.c_batch_stride = batch.stride_c;
     p.group_m = 16;
     p.c = c;
     p.ldc = d.ldc;
@@ -375,7 +410,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     p.c_vec4 = (aligned16(c) && d.ldc % 4 == 0) ? 1 : 0;
     p.wait_limit_ns = wait_limit_ns();
 
-    const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+    const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * nb;
     if (tiles > 0x7fffffffLL) return fail(MFB_EINVAL, "problem has too many output tiles");
     int dev = 0;
     cudaGetDevice(&dev);

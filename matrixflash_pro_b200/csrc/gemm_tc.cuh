@@ -5,8 +5,9 @@
 // B is MN-major (row-major B) or K-major (B stored transposed). K-major tiles are one
 // TMA box of 32 K x rows with 128B swizzle (16-byte atoms). MN-major tiles are
 // 32-element-wide column groups with the 128B/32-byte-atom swizzle that tcgen05
-// requires for MN-major TF32 operands. Each operand tensor map has an outer plane axis
-// (hi/lo planes in strict mode) so one TMA box brings both planes of a slab.
+// requires for MN-major TF32 operands. Each operand tensor map is 4-D: (cols, rows,
+// batch, plane), so one TMA box brings both planes (hi/lo in strict mode) of a slab of
+// one batch entry. Unbatched problems have batch = 1.
 #pragma once
 
 #include "tc_kernel.cuh"
@@ -17,6 +18,8 @@ struct GemmTcParams {
     int m, n, k;
     int num_kb;          // ceil(k / 32)
     int tiles_m, tiles_n;
+    int batch;           // strided-batched GEMMs: tiles of batch entry b follow those of b - 1
+    long long c_batch_stride;  // floats between consecutive C matrices
     int group_m;         // tile raster: group_m tile-rows walk N together
     float* c;
     long long ldc;
@@ -38,19 +41,22 @@ struct GemmProblem {
     static constexpr int kKSteps = kBK / 8;
 
     struct Tile {
-        int m0, n0;
+        int m0, n0, b;
     };
 
-    __device__ static int num_tiles(const Params& p) { return p.tiles_m * p.tiles_n; }
+    __device__ static int num_tiles(const Params& p) { return p.batch * p.tiles_m * p.tiles_n; }
     __device__ static int num_kb(const Params& p) { return p.num_kb; }
 
     __device__ static Tile tile(const Params& p, int t) {
+        const int per_batch = p.tiles_m * p.tiles_n;
+        const int b = t / per_batch;
+        t -= b * per_batch;
         const int per_group = p.group_m * p.tiles_n;
         const int group = t / per_group;
         const int first_m = group * p.group_m;
         const int gsize = min(p.group_m, p.tiles_m - first_m);
         const int in_group = t - group * per_group;
-        return Tile{(first_m + in_group % gsize) * kTcBM, (in_group / gsize) * BN};
+        return Tile{(first_m + in_group % gsize) * kTcBM, (in_group / gsize) * BN, b};
     }
 
     __device__ static int valid_cols(const Params& p, const Tile& t) { return min(BN, p.n - t.n0); }
@@ -60,15 +66,17 @@ struct GemmProblem {
         const int k0 = kb * kBK;
         if (A_MN) {
 #pragma unroll
-            for (int g = 0; g < kTcBM / 32; ++g) tma_load_3d(a_tile + g * PLANES * 4096, ta, bar, t.m0 + 32 * g, k0, 0);
+            for (int g = 0; g < kTcBM / 32; ++g)
+                tma_load_4d(a_tile + g * PLANES * 4096, ta, bar, t.m0 + 32 * g, k0, t.b, 0);
         } else {
-            tma_load_3d(a_tile, ta, bar, k0, t.m0, 0);
+            tma_load_4d(a_tile, ta, bar, k0, t.m0, t.b, 0);
         }
         if (B_MN) {
 #pragma unroll
-            for (int g = 0; g < BN / 32; ++g) tma_load_3d(b_tile + g * PLANES * 4096, tb, bar, t.n0 + 32 * g, k0, 0);
+            for (int g = 0; g < BN / 32; ++g)
+                tma_load_4d(b_tile + g * PLANES * 4096, tb, bar, t.n0 + 32 * g, k0, t.b, 0);
         } else {
-            tma_load_3d(b_tile, tb, bar, k0, t.n0, 0);
+            tma_load_4d(b_tile, tb, bar, k0, t.n0, t.b, 0);
         }
     }
 
@@ -92,7 +100,7 @@ struct GemmProblem {
         const int row = t.m0 + row_in_tile;
         if (row >= p.m) return;
         const int col0 = t.n0 + col0_in_tile;
-        float* crow = p.c + static_cast<long long>(row) * p.ldc;
+        float* crow = p.c + t.b * p.c_batch_stride + static_cast<long long>(row) * p.ldc;
         if (p.c_vec4 && col0 + COUNT <= p.n) {
             float4 cin[COUNT / 4];
             if (p.beta != 0.0f) {

@@ -306,6 +306,49 @@ MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream_h, const mfb_gemm
     return tc_gemm(d, cfgs[0], stream, a, b, c, bias, ws, need);
 }
 
+MFB_API mfb_status_t mfb_sgemm_strided_batched(int device, mfb_stream_t stream_h, const mfb_gemm_desc* desc,
+                                               const float* a, long long stride_a, const float* b,
+                                               long long stride_b, float* c, long long stride_c, int batch_count,
+                                               const float* bias) {
+    clear_error();
+    MFB_TRY(validate_desc(desc, a, b, c, bias, true));
+    const mfb_gemm_desc& d = *desc;
+    if (batch_count < 0) return fail(MFB_EINVAL, "batch count must be non-negative");
+    if (batch_count > 65535) return fail(MFB_EINVAL, "batch count must be at most 65535");
+    if (stride_a < 0 || stride_b < 0 || stride_c < 0) return fail(MFB_EINVAL, "batch strides must be non-negative");
+    if (batch_count == 0 || d.m == 0 || d.n == 0) return MFB_OK;
+    // Consecutive outputs may not overlap: C_i spans (m - 1) * ldc + n floats.
+    if (batch_count > 1 && stride_c < static_cast<long long>(d.m - 1) * d.ldc + d.n)
+        return fail(MFB_EINVAL, "stride_c makes the batch's outputs overlap");
+    if (batch_count > 1 && d.k > 0 && d.alpha != 0.0f) {
+        // No output may alias an input of any batch entry.
+        const long long a_rows = d.trans_a ? d.k : d.m, b_rows = d.trans_b ? d.n : d.k;
+        const float* a_end = a + stride_a * (batch_count - 1) + (a_rows - 1) * d.lda + (d.trans_a ? d.m : d.k);
+        const float* b_end = b + stride_b * (batch_count - 1) + (b_rows - 1) * d.ldb + (d.trans_b ? d.k : d.n);
+        const float* c_end = c + stride_c * (batch_count - 1) + static_cast<long long>(d.m - 1) * d.ldc + d.n;
+        if ((c < a_end && a < c_end) || (c < b_end && b < c_end))
+            return fail(MFB_EINVAL, "GEMM output cannot alias an input");
+    }
+    DeviceGuard guard;
+    MFB_TRY(select_device(device));
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_h);
+    if (d.k == 0 || d.alpha == 0.0f) {
+        for (int i = 0; i < batch_count; ++i) MFB_TRY(scale_output(d, stream, c + stride_c * i, bias));
+        return MFB_OK;
+    }
+    TcBatch batch;
+    batch.count = batch_count;
+    batch.stride_a = stride_a;
+    batch.stride_b = stride_b;
+    batch.stride_c = stride_c;
+    TcConfig cfgs[4];
+    if (tc_candidates(d, cfgs, 4, batch_count) == 0) return fail(MFB_EUNSUPPORTED, "no tcgen05 configuration");
+    const size_t need = tc_workspace_bytes(d, batch_count);
+    void* ws = nullptr;
+    MFB_TRY(stream_workspace(device, stream, need, &ws));
+    return tc_gemm(d, cfgs[0], stream, a, b, c, bias, ws, need, kPhaseAll, 0, batch);
+}
+
 MFB_API mfb_status_t mfb_gemv(int device, mfb_stream_t stream_h, const mfb_gemm_desc* desc, const float* a,
                               const float* b, float* c, const float* bias) {
     clear_error();

@@ -65,11 +65,20 @@ struct TcConfig {
 };
 
 // Admissible tile configurations for a problem, best-guess first.
-int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out);
+// Strided batch of GEMMs sharing one descriptor: entry i reads A + i*stride_a and
+// B + i*stride_b and writes C + i*stride_c (strides in floats).
+struct TcBatch {
+    int count = 1;
+    long long stride_a = 0, stride_b = 0, stride_c = 0;
+};
+
+// Tile configurations for `d`, best first. A batch of more than one GEMM uses the
+// single-CTA kernels only.
+int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch = 1);
 
 // Scratch the tcgen05 path needs for `d`: hi/lo planes of A and B (strict) or one
 // rounded TF32 plane of each (TF32), rows padded to 16 bytes.
-size_t tc_workspace_bytes(const mfb_gemm_desc& d);
+size_t tc_workspace_bytes(const mfb_gemm_desc& d, int batch = 1);
 
 // Runs the tcgen05 GEMM on `stream`: kPhasePrepare launches the split/round prepass of
 // the operands into `workspace`, kPhaseMultiply the GEMM kernel on the prepared
@@ -77,7 +86,7 @@ size_t tc_workspace_bytes(const mfb_gemm_desc& d);
 enum { kPhasePrepare = 1, kPhaseMultiply = 2, kPhaseAll = 3 };
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
-                     int phases = kPhaseAll, int sm_limit = 0);
+                     int phases = kPhaseAll, int sm_limit = 0, const TcBatch& batch = TcBatch());
 
 // cuTensorMapEncodeTiled for FP32 tensors of rank <= 5 (no interleave, L2 256B promotion,
 // zero fill out of bounds); strides_bytes has rank - 1 entries.
