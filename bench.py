@@ -217,6 +217,8 @@ AUX_WORKLOADS = {
     "conv_c4a": ("conv", (8, 3, 32, 32, 16)), "conv_c4b": ("conv", (256, 64, 56, 56, 64)),
     # strided-batched GEMM (batch_matmul): (batch, m, n, k); A, B ~ U[-1,1], alpha 1, beta 0.
     "bmm_b16_2048": ("bmm", (16, 2048, 2048, 2048)),
+    # column covariance of X (rows x cols) ~ N(1, 1): (rows, cols)
+    "cov_65536x2048": ("cov", (65536, 2048)),
 }
 
 
@@ -326,6 +328,43 @@ def run_aux_workload(args):
             return {"value": 2.0 * rows * n * k / dt / 1e12, "unit": "TFLOPS", "cores": info["worker_count"],
                     "kind": "reference" if impl == "reference" else "port",
                     "sample": f"{rows} rows of batch entry 0, gemm_f32 (the reference batches through cuBLAS only)"}
+    elif kind == "cov":
+        rows, cols = shape
+        X = torch.randn((rows, cols), device="cuda", generator=gen) + 1.0
+        work = 2.0 * cols * cols * rows  # the centered product X_c^T X_c
+        unit, metric_unit = "TFLOPS", 1e12
+        desc = f"covariance of a {rows}x{cols} matrix (X_c^T X_c / (rows-1); X is {rows * cols * 4 >> 20} MiB)"
+
+        def step():
+            mf.covariance(X, prec)
+
+        x_host = torch.empty_like(X, device="cpu").pin_memory()
+        x_host.copy_(X)
+        out_host = torch.empty((cols, cols), pin_memory=True)
+
+        def e2e_step():
+            X.copy_(x_host, non_blocking=True)
+            out_host.copy_(mf.covariance(X, prec), non_blocking=True)
+
+        h2d, d2h = X.numel() * 4, cols * cols * 4
+        passes = 6.0 if strict else 2.0
+        roof = {"bound": "tensor", "peak": peaks["bf16_tflops"] / passes, "unit": "TFLOP/s",
+                "peak_basis": f"bf16_tflops/{int(passes)} of {peak_src} MEASURED_PEAKS.json",
+                "kernel": "mean GEMV + tc_persistent_kernel (trans_a, centering fused in the split prepass)"}
+        launches = 6  # fill, GEMV partial + finish, split A, split B, GEMM
+
+        def cpu_sample():
+            sample_rows = 4096
+            xs = X[:sample_rows].cpu().numpy()
+            impl = "reference" if oracle.reference_available() else "restatement"
+            oracle.covariance_f32(xs, impl=impl)
+            t0 = time.perf_counter()
+            oracle.covariance_f32(xs, impl=impl)
+            dt = time.perf_counter() - t0
+            info = oracle.reference_info() if impl == "reference" else {"worker_count": 1}
+            return {"value": 2.0 * cols * cols * sample_rows / dt / 1e12, "unit": "TFLOPS",
+                    "cores": info["worker_count"], "kind": "reference" if impl == "reference" else "port",
+                    "sample": f"first {sample_rows} rows: oracle centering + the reference's gemm_f32"}
     else:
         nb, c, h, w, kf = shape
         x = torch.rand((nb, c, h, w), device="cuda", generator=gen) * 2 - 1

@@ -14,6 +14,8 @@
  *                                   src/ops/gemm/plan/implementation.inc:128-151
  *   mfb_sgemm_strided_batched       cublasSgemmStridedBatched in batch_matmul and its backward
  *                                   src/nn/batch.cu:12-35, src/nn/backward/batched_matmul.inc:7-55
+ *   mfb_covariance / mfb_correlation matrix_pro::covariance / correlation
+ *                                   src/ops/reductions/covariance.inc:23-60
  *   mfb_plan_*                      GemmPlan ctor/execute/tune/rows/cols/inner/candidate_count
  *                                   include/matrix_pro/ops/gemm.hpp:36-62
  *                                   (src/ops/gemm/plan/implementation.inc:5-152, tuning.inc:5-66)
@@ -183,6 +185,19 @@ MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream, const f
                                    float* scratch_c, int repeats, int* candidates_tested, float* best_ms);
 MFB_API mfb_status_t mfb_plan_info_get(mfb_plan_t plan, mfb_plan_info* info);
 MFB_API mfb_status_t mfb_plan_destroy(mfb_plan_t plan);
+
+/* ---------------------------------------------------------------- covariance / correlation */
+/* cov (cols x cols, row stride ldcov) = X_c^T X_c / max(rows - 1, 1), X_c = X minus its column
+ * means, X rows x cols with row stride ldx; correlation divides by sqrt(cov_ii cov_jj) (1 on the
+ * diagonal, 0 where a variance is not positive). Replaces matrix_pro::covariance / correlation
+ * (src/ops/reductions/covariance.inc:23-60; the product ran on cublasSgemm, :38-44). The means
+ * are one GEMV, the centering happens inside the GEMM's operand prepass, the product is the
+ * tcgen05 GEMM (precision: MFB_PRECISION_FP32 strict or MFB_PRECISION_TF32). rows or cols == 0:
+ * nothing is written. Scratch comes from the per-(device, stream) cache. */
+MFB_API mfb_status_t mfb_covariance(int device, mfb_stream_t stream, int rows, int cols, const float* x, int ldx,
+                                    float* cov, int ldcov, int precision);
+MFB_API mfb_status_t mfb_correlation(int device, mfb_stream_t stream, int rows, int cols, const float* x, int ldx,
+                                     float* corr, int ldcorr, int precision);
 
 /* ---------------------------------------------------------------- GEMV / skinny */
 /* Bandwidth-bound FP32 kernel for n <= 16 (y = A x with ldb/ldc strides) and for

@@ -2,7 +2,8 @@
 
 Drop-in for MatrixFlash-Pro's GEMM / GEMV / conv2d-forward hot path:
 ``cuda_gemm``/``cuda_sync`` (hw layer), ``GemmPlan``/``gemm``/``gemm_into``
-(Matrix API), ``gemv``, ``conv2d`` and the strided-batched ``batch_matmul`` family.
+(Matrix API), ``gemv``, ``conv2d``, the strided-batched ``batch_matmul`` family and
+``covariance``/``correlation``.
 All arithmetic runs in libmfb.so
 (hand-written tcgen05/TMA kernels); there is no CPU fallback.
 """
@@ -15,6 +16,7 @@ from .gemm import (GemmEpilogue, GemmOptions, GemmPlan, GemmPrecision, GemmTunin
 from .conv import conv2d, conv2d_into, conv2d_out_shape  # noqa: F401
 from .batch import (batch_matmul, batch_matmul_backward_left, batch_matmul_backward_right,  # noqa: F401
                     sgemm_strided_batched)
+from .stats import correlation, covariance  # noqa: F401
 from ._lib import LIB_PATH, lib  # noqa: F401
 
 __version__ = "0.1.0"

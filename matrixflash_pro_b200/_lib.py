@@ -22,7 +22,7 @@ EXPORTED_SYMBOLS = (
     "mfb_sgemm_noalloc", "mfb_sgemm_strided_batched",
     "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_set_sm_limit",
     "mfb_plan_tune", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
-    "mfb_conv2d_fwd", "mfb_naive_sgemm", "mfb_probe_wait_timeout",
+    "mfb_conv2d_fwd", "mfb_naive_sgemm", "mfb_probe_wait_timeout", "mfb_covariance", "mfb_correlation",
 )
 
 
@@ -63,6 +63,10 @@ def _declare(lib):
         "mfb_cuda_device_count": (st, [ctypes.POINTER(ctypes.c_int)]),
         "mfb_sgemm": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_sgemm_noalloc": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
+        "mfb_covariance": (st, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int,
+                                ctypes.c_int]),
+        "mfb_correlation": (st, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int,
+                                 ctypes.c_int]),
         "mfb_sgemm_strided_batched": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, ctypes.c_longlong, _vp,
                                            ctypes.c_longlong, _vp, ctypes.c_longlong, ctypes.c_int, _vp]),
         "mfb_plan_create": (st, [ctypes.c_int, ctypes.POINTER(GemmDesc), ctypes.POINTER(_vp)]),

@@ -29,10 +29,11 @@ __device__ __forceinline__ float round_tf32(float x) {
 // mode's operands, rounded to nearest like cuBLAS/CUTLASS TF32 conversion (the tensor
 // core itself would truncate the low 13 bits, a bias that shows on same-sign data).
 // blockIdx.y walks a strided batch: source matrix y at x + y * x_batch, its planes at
-// hi/lo + y * p_batch.
+// hi/lo + y * p_batch. shift (nullable, one value per stored column) is subtracted from
+// every element first: the column centering of covariance, fused into the split.
 __global__ void split_tf32_kernel(const float* __restrict__ x, long long ldx, int rows, int cols,
                                   float* __restrict__ hi, float* __restrict__ lo, long long ldp, int vec_in,
-                                  long long x_batch, long long p_batch) {
+                                  long long x_batch, long long p_batch, const float* __restrict__ shift) {
     x += blockIdx.y * x_batch;
     hi += blockIdx.y * p_batch;
     if (lo != nullptr) lo += blockIdx.y * p_batch;
@@ -50,6 +51,10 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, long long ldx, in
         } else {
 #pragma unroll
             for (int j = 0; j < 4; ++j) v[j] = (c0 + j < cols) ? __ldg(src + j) : 0.0f;
+        }
+        if (shift != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = (c0 + j < cols) ? v[j] - __ldg(shift + c0 + j) : 0.0f;
         }
         float4 h, l;
         if (lo != nullptr) {
@@ -331,7 +336,7 @@ mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c,
 
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
-                     int phases, int sm_limit, const TcBatch& batch) {
+                     int phases, int sm_limit, const TcBatch& batch, const TcPrologue& prologue) {
     const TcEntry* e = find_kernel(cfg);
     if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 kernel for this tile configuration");
     const int nb = batch.count;
@@ -352,6 +357,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         stored_dims(d, which == 0, &op.rows, &op.cols, &ld);
         const float* src = which == 0 ? a : b;
         const long long src_batch = which == 0 ? batch.stride_a : batch.stride_b;
+        const float* shift = which == 0 ? prologue.a_col_shift : prologue.b_col_shift;
         const long long ldp = round_up(op.cols, 4);
         const size_t pf = plane_floats(op.rows, op.cols);
         const size_t need = pf * 4 * static_cast<size_t>(cfg.planes) * static_cast<size_t>(nb);
@@ -367,7 +373,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         if (run_prepass && blocks > 0 && src != nullptr) {
             split_tf32_kernel<<<dim3(blocks, nb), 256, 0, stream>>>(src, ld, op.rows, op.cols, hi, lo, ldp,
                                                                     vec ? 1 : 0, src_batch,
-                                                                    static_cast<long long>(pf));
+                                                                    static_cast<long long>(pf), shift);
             MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");
         }
         op.base = hi;

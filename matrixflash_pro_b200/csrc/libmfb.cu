@@ -5,3 +5,4 @@
 #include "gemv.cu"
 #include "conv.cu"
 #include "noalloc.cu"
+#include "stats.cu"

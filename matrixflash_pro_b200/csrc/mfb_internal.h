@@ -72,6 +72,13 @@ struct TcBatch {
     long long stride_a = 0, stride_b = 0, stride_c = 0;
 };
 
+// Optional transform applied by the operand prepass: subtract shift[column of the stored
+// matrix] from every element of A and/or B before the TF32 split (covariance centering).
+struct TcPrologue {
+    const float* a_col_shift = nullptr;
+    const float* b_col_shift = nullptr;
+};
+
 // Tile configurations for `d`, best first. A batch of more than one GEMM uses the
 // single-CTA kernels only.
 int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch = 1);
@@ -86,7 +93,8 @@ size_t tc_workspace_bytes(const mfb_gemm_desc& d, int batch = 1);
 enum { kPhasePrepare = 1, kPhaseMultiply = 2, kPhaseAll = 3 };
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
-                     int phases = kPhaseAll, int sm_limit = 0, const TcBatch& batch = TcBatch());
+                     int phases = kPhaseAll, int sm_limit = 0, const TcBatch& batch = TcBatch(),
+                     const TcPrologue& prologue = TcPrologue());
 
 // cuTensorMapEncodeTiled for FP32 tensors of rank <= 5 (no interleave, L2 256B promotion,
 // zero fill out of bounds); strides_bytes has rank - 1 entries.

@@ -197,6 +197,48 @@ def conv2d_f64(x, w, bias, stride=1, padding=0):
     return y
 
 
+def col_mean_f32(x):
+    """Column means as the reference forms them: col_sum_kernel's four interleaved FP32
+    accumulators over rows 4i, 4i+1, 4i+2, 4i+3, the remainder into the first, combined as
+    (s0 + s1) + (s2 + s3) (src/ops/reductions/axis_kernels.cuh:25-45), then multiplied by
+    the float 1/rows (src/ops/reductions/covariance.inc:28)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    s = np.zeros((4, cols), np.float32)
+    full = rows // 4 * 4
+    for r in range(0, full, 4):
+        s += x[r:r + 4]
+    for r in range(full, rows):
+        s[0] += x[r]
+    total = (s[0] + s[1]) + (s[2] + s[3])
+    return total * np.float32(1.0 / np.float32(rows))
+
+
+def covariance_f32(x, impl="restatement"):
+    """matrix_pro::covariance (src/ops/reductions/covariance.inc:23-47) on the CPU: center the
+    columns (center_columns_kernel, moment_kernels.cuh:5-10), then
+    (1/max(rows-1, 1)) * X_c^T X_c with gemm_f32 standing in for the reference's cublasSgemm."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    xc = x - col_mean_f32(x)[None, :]
+    xt = np.ascontiguousarray(xc.T)
+    out = np.zeros(cols * cols, np.float32)
+    alpha = float(np.float32(1.0) / np.float32(rows - 1 if rows > 1 else 1))
+    gemm_f32(cols, cols, rows, xt, rows, xc, cols, out, cols, alpha, 0.0, impl=impl)
+    return out.reshape(cols, cols)
+
+
+def correlation_f32(cov):
+    """covariance_to_correlation_kernel (src/ops/reductions/moment_kernels.cuh:51-67)."""
+    cov = np.asarray(cov, np.float32)
+    d = np.diag(cov).astype(np.float32)
+    denom = np.sqrt((d[:, None] * d[None, :]).astype(np.float32)).astype(np.float32)
+    ok = (d[:, None] > 0) & (d[None, :] > 0)
+    corr = np.where(ok, cov / np.where(ok, denom, np.float32(1.0)), np.float32(0.0)).astype(np.float32)
+    np.fill_diagonal(corr, 1.0)
+    return corr
+
+
 def epilogue_f32(c, ldc, bias, m, n, mode):
     """In-place column-bias epilogue (mode 0 bias, 1 bias+ReLU, 2 bias+tanh-GELU)."""
     bias = np.ascontiguousarray(bias, dtype=np.float32)
