@@ -17,6 +17,7 @@ namespace mfb {
 namespace {
 
 constexpr int kConvThreads = 256;
+constexpr double kConvDirectMaxFlops = 1e7;  // below this the direct kernel beats the tcgen05 path
 
 __device__ __forceinline__ float conv_round_tf32(float x) {
     uint32_t r;
@@ -39,6 +40,74 @@ __device__ __forceinline__ void write_planes4(float* hi, float* lo, long long of
 }
 
 // x (N,C,H,W) -> X [N][Hp*Wp][Cp]: zero border of `pad`, zero channels in [C, Cp).
+// grid (ceil(Hp / kPackRows), ceil(Cp / 32), N): a block takes kPackRows padded rows of
+// 32 channels. Input rows are read whole (128-bit loads when W and the row base allow),
+// transposed in shared memory (odd row stride: conflict-free column reads) and written
+// as 128-byte channel rows of every padded position, border zeros included.
+constexpr int kPackRows = 2;
+constexpr int kPackMaxWp = 512;  // padded width the shared tile holds; wider images use the generic kernel
+
+__global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __restrict__ x, int c, int h, int w,
+                                                             int pad, int cp, int hp, int wp, int vec,
+                                                             float* __restrict__ hi, float* __restrict__ lo) {
+    extern __shared__ float tile[];  // [32][stride], stride = kPackRows * wp rounded up to odd
+    const int stride = (kPackRows * wp) | 1;
+    const int pr0 = blockIdx.x * kPackRows;
+    const int c0 = blockIdx.y * 32;
+    const int img = blockIdx.z;
+    const int rows = min(kPackRows, hp - pr0);
+    // Phase 1: input rows -> tile (zeros for border columns, border rows and channels >= C).
+    const int w4 = vec ? w / 4 : 0;
+    for (int i = threadIdx.x; i < 32 * rows * wp; i += blockDim.x) {
+        const int cc = i / (rows * wp);
+        const int rem = i - cc * rows * wp;
+        tile[cc * stride + rem] = 0.0f;
+    }
+    __syncthreads();
+    if (vec) {
+        for (int i = threadIdx.x; i < 32 * rows * w4; i += blockDim.x) {
+            const int cc = i / (rows * w4);
+            const int rem = i - cc * rows * w4;
+            const int rr = rem / w4;
+            const int q4 = rem - rr * w4;
+            const int ih = pr0 + rr - pad, ch = c0 + cc;
+            if (ih >= 0 && ih < h && ch < c) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(
+                    x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + 4 * q4));
+                float* dst = tile + cc * stride + rr * wp + pad + 4 * q4;
+                dst[0] = v.x;
+                dst[1] = v.y;
+                dst[2] = v.z;
+                dst[3] = v.w;
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < 32 * rows * w; i += blockDim.x) {
+            const int cc = i / (rows * w);
+            const int rem = i - cc * rows * w;
+            const int rr = rem / w;
+            const int iw = rem - rr * w;
+            const int ih = pr0 + rr - pad, ch = c0 + cc;
+            if (ih >= 0 && ih < h && ch < c)
+                tile[cc * stride + rr * wp + pad + iw] =
+                    __ldg(x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + iw);
+        }
+    }
+    __syncthreads();
+    // Phase 2: one float4 of 4 channels per (position, group); 8 groups cover 32 channels.
+    const long long npos = static_cast<long long>(hp) * wp;
+    const int groups = min(8, (cp - c0) / 4);
+    for (int i = threadIdx.x; i < rows * wp * 8; i += blockDim.x) {
+        const int pos = i / 8, q = i % 8;
+        if (q >= groups) continue;
+        const long long off = (static_cast<long long>(img) * npos + static_cast<long long>(pr0) * wp + pos) * cp +
+                              c0 + 4 * q;
+        const float* t = tile + 4 * q * stride + pos;
+        write_planes4(hi, lo, off, t[0], t[stride], t[2 * stride], t[3 * stride]);
+    }
+}
+
+// Generic version of the same layout change (any padded width): 32 channels x 64 positions per block.
 // grid (ceil(Hp*Wp / 64), ceil(Cp / 32), N): a 32-channel x 64-position tile is read
 // along positions (coalesced in W) and written as 128-byte channel rows.
 __global__ void __launch_bounds__(256) conv_pack_input_kernel(const float* __restrict__ x, int c, int h, int w,
@@ -201,7 +270,13 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
     const int P = (h + 2 * pad - r) / stride + 1;
     const int Q = (w + 2 * pad - s) / stride + 1;
     if (n == 0 || P <= 0 || Q <= 0) return MFB_OK;
-    if (stride != 1) return conv2d_direct(stream, n, c, h, w, k, r, s, stride, pad, P, Q, x, wgt, bias, y);
+    // Other strides, and problems too small to amortize the tensor path's three launches and
+    // pipeline fill (~25 us; e.g. 8x3x32x32 with 16 filters, 7 MFLOP): the direct kernel,
+    // one launch, FP32 FMA chains in the reference's order (at least as accurate as either
+    // precision policy asks).
+    const double flops = 2.0 * n * k * P * Q * static_cast<double>(c) * r * s;
+    if (stride != 1 || flops < kConvDirectMaxFlops)
+        return conv2d_direct(stream, n, c, h, w, k, r, s, stride, pad, P, Q, x, wgt, bias, y);
 
     const int planes = precision == MFB_PRECISION_FP32 ? 2 : 1;
     const int cp = (c + 3) / 4 * 4;
@@ -221,8 +296,20 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
     float* b_hi = a_hi + planes * a_plane;
     float* b_lo = planes == 2 ? b_hi + b_plane : nullptr;
 
-    dim3 pgrid(static_cast<unsigned>((npos + 63) / 64), static_cast<unsigned>((cp + 31) / 32), n);
-    conv_pack_input_kernel<<<pgrid, 256, 0, stream>>>(x, c, h, w, pad, cp, hp, wp, a_hi, a_lo);
+    if (wp <= kPackMaxWp) {
+        const size_t tile_bytes = static_cast<size_t>(32) * ((kPackRows * wp) | 1) * 4;
+        if (tile_bytes > 48 * 1024)
+            MFB_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(&conv_pack_rows_kernel),
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(tile_bytes)),
+                         "conv prepass smem attribute");
+        const int vec = (w % 4 == 0 && aligned16(x)) ? 1 : 0;
+        dim3 pgrid(static_cast<unsigned>((hp + kPackRows - 1) / kPackRows), static_cast<unsigned>((cp + 31) / 32), n);
+        conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, pad, cp, hp, wp, vec, a_hi, a_lo);
+    } else {
+        dim3 pgrid(static_cast<unsigned>((npos + 63) / 64), static_cast<unsigned>((cp + 31) / 32), n);
+        conv_pack_input_kernel<<<pgrid, 256, 0, stream>>>(x, c, h, w, pad, cp, hp, wp, a_hi, a_lo);
+    }
     MFB_CUDA_TRY(cudaGetLastError(), "conv input prepass launch");
     const long long wgroups = static_cast<long long>(r) * s * k * (cp / 4);
     conv_pack_weights_kernel<<<static_cast<int>(std::min<long long>((wgroups + 255) / 256, 148LL * 4)), 256, 0,

@@ -43,6 +43,7 @@ template <int BN_, int PLANES_>
 struct ConvProblem {
     using Params = ConvTcParams;
     static constexpr int BN = BN_, PLANES = PLANES_, A_MN = 0, B_MN = 0;
+    static constexpr bool kStackB = PLANES_ == 2 && BN_ <= 64;  // K-major weight tiles: hi, lo rows adjacent
     static constexpr int STAGES = conv_stages<BN_, PLANES_>();
     static constexpr int kATileBytes = PLANES * kTcBM * 128;
     static constexpr int kBTileBytes = PLANES * BN * 128;

@@ -36,6 +36,7 @@ template <int BN_, int STAGES_, int PLANES_, int A_MN_, int B_MN_>
 struct GemmProblem {
     using Params = GemmTcParams;
     static constexpr int BN = BN_, STAGES = STAGES_, PLANES = PLANES_, A_MN = A_MN_, B_MN = B_MN_;
+    static constexpr bool kStackB = false;  // row-major B is MN-major: its planes interleave per 32 columns
     static constexpr int kATileBytes = PLANES * kTcBM * kBK * 4;
     static constexpr int kBTileBytes = PLANES * BN * kBK * 4;
     static constexpr int kKSteps = kBK / 8;

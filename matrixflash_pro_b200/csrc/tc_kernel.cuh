@@ -49,12 +49,24 @@ __device__ __forceinline__ float apply_epilogue_op(float v, const float* bias, i
     return v;
 }
 
+// Strict mode with stacked B (Prob::kStackB, K-major B tiles of at most 64 rows): the hi
+// and lo planes of a B tile lie back to back in shared memory, so they form one N = 2*BN
+// operand. Each K step then issues two MMAs, A_hi x [B_hi | B_lo] and A_lo x [B_hi | B_lo],
+// instead of three N = BN ones (lo*lo is a harmless extra term): a tcgen05 TF32 MMA with
+// M = 128 costs about the same for N = 32, 64 or 128 (measured ~38 ns), so narrow tiles
+// are issue-bound and stacking cuts their MMA time by a third. The accumulator is 2*BN
+// columns wide and the epilogue adds its two halves.
+template <class Prob>
+constexpr int tc_acc_cols() {
+    return Prob::kStackB ? 2 * Prob::BN : Prob::BN;
+}
+
 template <class Prob>
 struct TcLayout {
     static constexpr int kStageBytes = Prob::kATileBytes + Prob::kBTileBytes;
     static constexpr int kBarrierOffset = Prob::STAGES * kStageBytes;
     static constexpr int kBytes = kBarrierOffset + 256 + 1024;  // barriers + 1 KiB alignment slack
-    static constexpr int kTmemCols = 2 * Prob::BN < 32 ? 32 : 2 * Prob::BN;
+    static constexpr int kTmemCols = 2 * tc_acc_cols<Prob>() < 32 ? 32 : 2 * tc_acc_cols<Prob>();
     static constexpr int kEpiWarps = Prob::PLANES == 2 ? 8 : 4;
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };
@@ -74,6 +86,93 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* out) {
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 8; ++j) out[j] = __uint_as_float(r[j]);
+    }
+}
+
+// Epilogue role (warps 2..) shared by the persistent tcgen05 kernels: waits for each
+// finished accumulator (a tile in TF32 mode, a 64-deep K chunk in strict mode, summed in
+// registers with round-to-nearest adds), hands the TMEM buffer back to the MMA issuer and
+// writes the tile through Prob::store.
+template <class Prob>
+__device__ __forceinline__ void tc_epilogue_role(const typename Prob::Params& p, uint32_t tmem_base,
+                                                 uint64_t* acc_full_bar, uint64_t* acc_empty_bar,
+                                                 volatile int* abort_flag, uint64_t limit, int warp, int lane) {
+    constexpr int BN = Prob::BN;
+    constexpr int PLANES = Prob::PLANES;
+    constexpr int ACC = tc_acc_cols<Prob>();  // accumulator columns per buffer
+    const int num_tiles = Prob::num_tiles(p);
+    const int num_kb = Prob::num_kb(p);
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int row = quarter * 32 + lane;  // row within the tile
+    int buf = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const typename Prob::Tile tile = Prob::tile(p, t);
+        const int valid = Prob::valid_cols(p, tile);
+        if constexpr (PLANES == 2) {
+            // Round-to-nearest FP32 sum of the K chunks, in registers: this warp owns
+            // columns [half * BN/2, (half + 1) * BN/2) of the tile.
+            constexpr int kCols = BN / 2;
+            constexpr int kStep = kCols % 16 == 0 ? 16 : 8;
+            const int half = (warp - 2) >> 2;
+            float sum[kCols];
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
+            const int n_chunks = (num_kb + kChunkKb - 1) / kChunkKb;
+            for (int c = 0; c < n_chunks; ++c, ++buf) {
+                const int b = buf & 1;
+                if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
+                    report_status(kStatusTimeoutEpilogue, abort_flag);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int q = 0; q < kCols / kStep; ++q) {
+                    float v[kStep];
+                    tmem_load_cols<kStep>(tmem_base + lane_base + b * ACC + half * kCols + q * kStep, v);
+                    if constexpr (Prob::kStackB) {
+                        // second half: the products with B_lo
+                        float w[kStep];
+                        tmem_load_cols<kStep>(tmem_base + lane_base + b * ACC + BN + half * kCols + q * kStep, w);
+#pragma unroll
+                        for (int j = 0; j < kStep; ++j) v[j] += w[j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < kStep; ++j) sum[q * kStep + j] += v[j];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
+            }
+            if (!ok) break;
+#pragma unroll
+            for (int q = 0; q < kCols / kStep; ++q) {
+                const int col0 = half * kCols + q * kStep;
+                if (col0 < valid) Prob::template store<kStep>(p, tile, row, col0, &sum[q * kStep]);
+            }
+        } else {
+            const int b = buf & 1;
+            if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
+                report_status(kStatusTimeoutEpilogue, abort_flag);
+                break;
+            }
+            tc_fence_after();
+            const int nq = (min(valid, BN) + 15) / 16;
+            for (int q = 0; q < nq; ++q) {
+                float v[16];
+                tmem_load_cols<16>(tmem_base + lane_base + b * BN + q * 16, v);
+                if (q == nq - 1) {
+                    // Accumulator fully read: hand it back to the MMA issuer.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
+                }
+                Prob::template store<16>(p, tile, row, q * 16, v);
+            }
+            ++buf;
+        }
     }
 }
 
@@ -157,6 +256,7 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------ MMA issuer
         constexpr uint32_t idesc = umma_idesc_tf32(kTcBM, BN, Prob::A_MN, Prob::B_MN);
+        constexpr uint32_t idesc_stacked = umma_idesc_tf32(kTcBM, 2 * BN, Prob::A_MN, Prob::B_MN);
         // Accumulator buffers are handed out per tile (tf32) or per K chunk (strict).
         const int kb_per_buf = PLANES == 2 ? kChunkKb : 0x7fffffff;
         int it = 0;   // K blocks consumed (stage ring position)
@@ -174,7 +274,7 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    d_tmem = tmem_base + b * BN;
+                    d_tmem = tmem_base + b * tc_acc_cols<Prob>();
                     acc = 0;
                 }
                 const int s = it % STAGES;
@@ -190,6 +290,13 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
                 for (int ks = 0; ks < Prob::kKSteps; ++ks) {
                     const uint64_t a_hi = Prob::a_desc(a_addr, 0, ks);
                     const uint64_t b_hi = Prob::b_desc(b_addr, 0, ks);
+                    if constexpr (Prob::kStackB) {
+                        // b_hi spans both planes: 2*BN rows [B_hi; B_lo]
+                        umma_tf32(d_tmem, a_hi, b_hi, idesc_stacked, acc);
+                        umma_tf32(d_tmem, Prob::a_desc(a_addr, 1, ks), b_hi, idesc_stacked, 1);
+                        acc = 1;
+                        continue;
+                    }
                     if (PLANES == 2) {
                         umma_tf32(d_tmem, Prob::a_desc(a_addr, 1, ks), b_hi, idesc, acc);
                         acc = 1;
@@ -209,72 +316,7 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
         umma_commit(drain_bar);
         if (!mbar_wait_drain(drain_bar, 0, limit)) report_status(kStatusTimeoutDrain, nullptr);
     } else if (warp >= 2) {
-        // ------------------------------------------------------------ epilogue
-        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
-        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-        const int row = quarter * 32 + lane;  // row within the tile
-        int buf = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-            const typename Prob::Tile tile = Prob::tile(p, t);
-            const int valid = Prob::valid_cols(p, tile);
-            if constexpr (PLANES == 2) {
-                // Round-to-nearest FP32 sum of the K chunks, in registers: this warp owns
-                // columns [half * BN/2, (half + 1) * BN/2) of the tile.
-                constexpr int kCols = BN / 2;
-                constexpr int kStep = kCols % 16 == 0 ? 16 : 8;
-                const int half = (warp - 2) >> 2;
-                float sum[kCols];
-#pragma unroll
-                for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
-                const int n_chunks = (num_kb + kChunkKb - 1) / kChunkKb;
-                for (int c = 0; c < n_chunks; ++c, ++buf) {
-                    const int b = buf & 1;
-                    if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
-                        report_status(kStatusTimeoutEpilogue, abort_flag);
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-#pragma unroll
-                    for (int q = 0; q < kCols / kStep; ++q) {
-                        float v[kStep];
-                        tmem_load_cols<kStep>(tmem_base + lane_base + b * BN + half * kCols + q * kStep, v);
-#pragma unroll
-                        for (int j = 0; j < kStep; ++j) sum[q * kStep + j] += v[j];
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
-                }
-                if (!ok) break;
-#pragma unroll
-                for (int q = 0; q < kCols / kStep; ++q) {
-                    const int col0 = half * kCols + q * kStep;
-                    if (col0 < valid) Prob::template store<kStep>(p, tile, row, col0, &sum[q * kStep]);
-                }
-            } else {
-                const int b = buf & 1;
-                if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
-                    report_status(kStatusTimeoutEpilogue, abort_flag);
-                    break;
-                }
-                tc_fence_after();
-                const int nq = (min(valid, BN) + 15) / 16;
-                for (int q = 0; q < nq; ++q) {
-                    float v[16];
-                    tmem_load_cols<16>(tmem_base + lane_base + b * BN + q * 16, v);
-                    if (q == nq - 1) {
-                        // Accumulator fully read: hand it back to the MMA issuer.
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
-                    }
-                    Prob::template store<16>(p, tile, row, q * 16, v);
-                }
-                ++buf;
-            }
-        }
+        tc_epilogue_role<Prob>(p, tmem_base, acc_full_bar, acc_empty_bar, abort_flag, limit, warp, lane);
     }
 
     tc_fence_before();

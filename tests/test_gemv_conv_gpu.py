@@ -149,7 +149,17 @@ def test_conv_known_answers():
 
 @pytest.mark.parametrize("n,c,h,w,k,r,s,stride,pad", [
     (2, 64, 56, 56, 64, 3, 3, 1, 1), (3, 7, 13, 11, 5, 3, 3, 1, 1), (1, 16, 20, 24, 32, 5, 5, 2, 2),
-    (2, 3, 9, 9, 4, 1, 1, 1, 0), (1, 33, 17, 15, 48, 3, 1, 1, 1)])
+    (2, 3, 9, 9, 4, 1, 1, 1, 0), (1, 33, 17, 15, 48, 3, 1, 1, 1),
+    # wide rows (a 128-position tile spans less than two padded rows); 200 filters: one
+    # 256-wide filter tile (no stacked B); 160 filters: BN = 256 as well
+    (8, 8, 8, 100, 16, 3, 3, 1, 1), (2, 40, 6, 130, 200, 3, 3, 1, 1), (1, 32, 12, 12, 160, 3, 3, 1, 1),
+    # BN = 32 and BN = 128 filter tiles (stacked B only up to 64 filters)
+    (8, 16, 20, 20, 24, 3, 3, 1, 1), (1, 64, 14, 14, 128, 3, 3, 1, 1),
+    # padded width beyond the row-wise prepass tile: the generic 64-position prepass
+    (16, 4, 3, 520, 8, 3, 3, 1, 1),
+    # odd channels / widths / filter counts above the direct-kernel cutoff (1e7 FLOP): tcgen05 path
+    (8, 7, 33, 31, 40, 3, 3, 1, 1), (8, 33, 17, 15, 48, 3, 1, 1, 1), (64, 32, 20, 20, 64, 1, 1, 1, 0),
+    (3, 5, 45, 37, 19, 5, 5, 1, 2)])
 def test_conv_seeded_against_restatement(n, c, h, w, k, r, s, stride, pad):
     x = oracle.seeded((n, c, h, w), seed=c)
     wt = oracle.seeded((k, c, r, s), "normal", seed=k, scale=float(np.sqrt(2.0 / (c * r * s))))
