@@ -222,6 +222,18 @@ AUX_WORKLOADS = {
 }
 
 
+def tf32_mma_fields(mf, device, achieved, strict):
+    """The TF32 MMA rate measured on this GPU after the timed region (N = 256 MMAs from reused
+    shared-memory operands: the tensor pipe's own ceiling, above the bf16/2 derivation) and the
+    achieved rate as a fraction of it (strict = 3 TF32 passes)."""
+    try:
+        peak = mf.probe_tf32_mma_tflops(256, device)
+    except Exception as exc:  # diagnostic only
+        return {"peak_tf32_mma_measured": f"failed: {exc}"}
+    frac = achieved / (peak / (3.0 if strict else 1.0)) if achieved and peak > 0 else None
+    return {"peak_tf32_mma_measured": peak, "frac_vs_tf32_mma_measured": frac}
+
+
 def run_aux_workload(args):
     """GEMV and conv2d workloads: one GPU per process (N > 1 runs independent replicas)."""
     import torch
@@ -421,6 +433,8 @@ def run_aux_workload(args):
     value = work * args.steps / (ms / 1e3) / metric_unit
     roof.update({"achieved": value, "frac": value / roof["peak"], "traffic": read_profile_traffic(
         f"{args.workload}_{args.precision}" if kind == "conv" else args.workload)})
+    if roof["bound"] == "tensor" and rank == 0:
+        roof.update(tf32_mma_fields(mf, local, value, strict))
     e2e = None
     if args.e2e_steps > 0:
         e2e_step()
@@ -606,6 +620,8 @@ def main():
                 "peak_burst": peak_burst, "peak_sustained": peak_sust,
                 "kernel_ms_per_launch": kernel_ms / max(1, launches_gemm),
                 "flops_per_launch": gemm_flops / max(1, launches_gemm)}
+    if rank == 0:
+        roofline.update(tf32_mma_fields(mf, local, achieved, strict))
 
     # ---------------------------------------------------------------- CPU baseline (rank 0, N=1)
     cpu = None

@@ -221,6 +221,12 @@ MFB_API mfb_status_t mfb_naive_sgemm(int device, mfb_stream_t stream, const mfb_
                                      const float* b, float* c, const float* bias);
 
 /* ---------------------------------------------------------------- failure-path probe */
+/* Diagnostic (no reference counterpart): the TF32 tcgen05 MMA rate of `device` in TFLOP/s,
+ * measured with back-to-back M = 128, N = n (64, 128 or 256), K = 8 MMAs on every SM from
+ * reused shared-memory operands: the tensor pipe's ceiling for roofline denominators (a
+ * streaming kernel also pays for operand fetch). Synchronous; takes a few milliseconds. */
+MFB_API mfb_status_t mfb_probe_tf32_mma_tflops(int device, int n, float* tflops);
+
 /* Launches a kernel that waits on an mbarrier nothing arrives on, bounded by
  * limit_ns; it records kStatusTimeoutProbe in the status word and returns. Used by
  * tests to exercise the timeout path without faulting or hanging the GPU. */

@@ -11,7 +11,8 @@ from .errors import (CudaError, DeviceTimeoutError, InvalidArgumentError, Matrix
                      ShapeMismatchError)
 from .gemm import (GemmEpilogue, GemmOptions, GemmPlan, GemmPrecision, GemmTuningResult, checked_dim, cuda_gemm,  # noqa: F401,E501
                    cuda_sync, device_status, gemm, gemm_bias_gelu, gemm_bias_relu, gemm_into, gemv,
-                   get_wait_limit_ns, make_desc, multiply, multiply_into, naive_sgemm, set_wait_limit_ns, sgemm,
+                   get_wait_limit_ns, make_desc, multiply, multiply_into, naive_sgemm, probe_tf32_mma_tflops,
+                   set_wait_limit_ns, sgemm,
                    sgemm_ptr, sync)
 from .conv import conv2d, conv2d_into, conv2d_out_shape  # noqa: F401
 from .batch import (batch_matmul, batch_matmul_backward_left, batch_matmul_backward_right,  # noqa: F401

@@ -6,3 +6,4 @@
 #include "conv.cu"
 #include "noalloc.cu"
 #include "stats.cu"
+#include "peak_probe.cu"

@@ -120,6 +120,15 @@ def sync(device: int | None = None, stream=None) -> None:
     _lib.check(_lib.lib().mfb_sync(dev, _stream_handle(stream)), "sync")
 
 
+def probe_tf32_mma_tflops(n: int = 256, device: int | None = None) -> float:
+    """Measured TF32 tcgen05 MMA rate (TFLOP/s) of the device: back-to-back M=128, N=n, K=8
+    MMAs on every SM from reused shared-memory operands (the tensor pipe's ceiling)."""
+    dev = torch.cuda.current_device() if device is None else device
+    out = ctypes.c_float(0.0)
+    _lib.check(_lib.lib().mfb_probe_tf32_mma_tflops(dev, int(n), ctypes.byref(out)), "probe_tf32_mma_tflops")
+    return float(out.value)
+
+
 def device_status(device: int | None = None) -> int:
     """Read and clear the device status word (0 = no bounded wait gave up)."""
     dev = torch.cuda.current_device() if device is None else device

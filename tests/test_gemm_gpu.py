@@ -317,3 +317,14 @@ def test_prepare_operands_one_at_a_time(precision):
     assert torch.equal(got, want)
     with pytest.raises(mf.InvalidArgumentError):
         _lib.check(lib.mfb_plan_prepare(h, s, 0, 0), "prepare nothing")
+
+
+def test_tf32_mma_rate_probe():
+    """The diagnostic TF32 MMA-rate probe returns a plausible B200 figure and leaves no status bit."""
+    peak256 = mf.probe_tf32_mma_tflops(256)
+    peak64 = mf.probe_tf32_mma_tflops(64)
+    assert 300.0 < peak256 < 1500.0, peak256
+    assert 0.0 < peak64 < peak256  # narrow MMAs cost nearly as long as wide ones
+    assert mf.device_status() == 0
+    with pytest.raises(mf.InvalidArgumentError):
+        mf.probe_tf32_mma_tflops(96)
