@@ -215,6 +215,8 @@ AUX_WORKLOADS = {
     "gemv_n1": ("gemv", 1), "gemv_n4": ("gemv", 4), "gemv_n8": ("gemv", 8), "gemv_n16": ("gemv", 16),
     # conv2d forward, stride 1, pad 1, 3x3: (N, C, H, W, K); x ~ U[-1,1], w ~ N(0, 2/fan_in), bias 0.
     "conv_c4a": ("conv", (8, 3, 32, 32, 16)), "conv_c4b": ("conv", (256, 64, 56, 56, 64)),
+    # conv2d backward of the same shape: input, weight and bias gradients per step
+    "conv_c4b_bwd": ("conv_bwd", (256, 64, 56, 56, 64)),
     # strided-batched GEMM (batch_matmul): (batch, m, n, k); A, B ~ U[-1,1], alpha 1, beta 0.
     "bmm_b16_2048": ("bmm", (16, 2048, 2048, 2048)),
     # column covariance of X (rows x cols) ~ N(1, 1): (rows, cols)
@@ -377,6 +379,50 @@ def run_aux_workload(args):
             return {"value": 2.0 * cols * cols * sample_rows / dt / 1e12, "unit": "TFLOPS",
                     "cores": info["worker_count"], "kind": "reference" if impl == "reference" else "port",
                     "sample": f"first {sample_rows} rows: oracle centering + the reference's gemm_f32"}
+    elif kind == "conv_bwd":
+        nb, c, h, w, kf = shape
+        x = torch.rand((nb, c, h, w), device="cuda", generator=gen) * 2 - 1
+        wt = torch.randn((kf, c, 3, 3), device="cuda", generator=gen) * float(np.sqrt(2.0 / (c * 9)))
+        g = torch.randn((nb, kf, h, w), device="cuda", generator=gen)
+        work = 2 * 2.0 * nb * kf * h * w * c * 9  # dx and dw: one forward-sized contraction each
+        unit, metric_unit = "TFLOPS", 1e12
+        desc = f"conv2d backward (dx, dw, db) NCHW {nb}x{c}x{h}x{w}, {kf} 3x3 filters, stride 1, pad 1"
+
+        def step():
+            mf.conv2d_input_backward(g, x, wt, 1, 1, prec)
+            mf.conv2d_weight_backward(g, x, wt, 1, 1, prec)
+            mf.conv2d_bias_backward(g)
+
+        g_h = torch.empty_like(g, device="cpu").pin_memory()
+        x_h = torch.empty_like(x, device="cpu").pin_memory()
+        g_h.copy_(g)
+        x_h.copy_(x)
+
+        def e2e_step():
+            g.copy_(g_h, non_blocking=True)
+            x.copy_(x_h, non_blocking=True)
+            dx = mf.conv2d_input_backward(g, x, wt, 1, 1, prec)
+            dw = mf.conv2d_weight_backward(g, x, wt, 1, 1, prec)
+            mf.conv2d_bias_backward(g)
+            dx.cpu()
+            dw.cpu()
+
+        h2d, d2h = (g.numel() + x.numel()) * 4, (x.numel() + wt.numel()) * 4
+        passes = 6.0 if strict else 2.0
+        roof = {"bound": "tensor", "peak": peaks["bf16_tflops"] / passes, "unit": "TFLOP/s",
+                "peak_basis": f"bf16_tflops/{int(passes)} of {peak_src} MEASURED_PEAKS.json",
+                "kernel": "dx: tc_persistent_kernel<ConvProblem> on flipped filters; dw: tc_persistent_kernel"
+                          "<ConvWgradProblem> split over positions + fixed-order reduce (time includes prepasses)"}
+        launches = 10  # dx: 2 prepasses + GEMM; dw: 2 prepasses + GEMM + reduce; db: 1 (+ the output allocation)
+
+        def cpu_sample():
+            xs, gs, ws = x[:1].cpu().numpy(), g[:1].cpu().numpy(), wt.cpu().numpy()
+            t0 = time.perf_counter()
+            oracle.conv2d_input_backward(gs, ws, xs.shape, 1, 1)
+            oracle.conv2d_weight_backward(gs, xs, ws.shape, 1, 1)
+            dt = time.perf_counter() - t0
+            return {"value": 2 * 2.0 * kf * h * w * c * 9 / dt / 1e12, "unit": "TFLOPS", "cores": 1, "kind": "port",
+                    "sample": "1 image, single-thread restatements of the reference's backward kernels"}
     else:
         nb, c, h, w, kf = shape
         x = torch.rand((nb, c, h, w), device="cuda", generator=gen) * 2 - 1
@@ -432,7 +478,7 @@ def run_aux_workload(args):
     mf.sync()
     value = work * args.steps / (ms / 1e3) / metric_unit
     roof.update({"achieved": value, "frac": value / roof["peak"], "traffic": read_profile_traffic(
-        f"{args.workload}_{args.precision}" if kind == "conv" else args.workload)})
+        f"{args.workload}_{args.precision}" if kind in ("conv", "conv_bwd") else args.workload)})
     if roof["bound"] == "tensor" and rank == 0:
         roof.update(tf32_mma_fields(mf, local, value, strict))
     e2e = None

@@ -14,6 +14,9 @@
  *                                   src/ops/gemm/plan/implementation.inc:128-151
  *   mfb_sgemm_strided_batched       cublasSgemmStridedBatched in batch_matmul and its backward
  *                                   src/nn/batch.cu:12-35, src/nn/backward/batched_matmul.inc:7-55
+ *   mfb_conv2d_bwd_data / _filter /  conv2d_input_backward / conv2d_weight_backward / conv2d_bias_backward
+ *   mfb_conv2d_bwd_bias             include/matrix_pro/nn/conv.hpp:25-29 (kernels:
+ *                                   src/nn/backward/convolution_kernels.cuh:9-95)
  *   mfb_covariance / mfb_correlation matrix_pro::covariance / correlation
  *                                   src/ops/reductions/covariance.inc:23-60
  *   mfb_plan_*                      GemmPlan ctor/execute/tune/rows/cols/inner/candidate_count
@@ -185,6 +188,24 @@ MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream, const f
                                    float* scratch_c, int repeats, int* candidates_tested, float* best_ms);
 MFB_API mfb_status_t mfb_plan_info_get(mfb_plan_t plan, mfb_plan_info* info);
 MFB_API mfb_status_t mfb_plan_destroy(mfb_plan_t plan);
+
+/* ---------------------------------------------------------------- conv2d backward */
+/* Gradients of mfb_conv2d_fwd (same n, c, h, w, k, r, s, stride, pad; P, Q as there), NCHW:
+ * dx (N,C,H,W) = dL/dx from dy (N,K,P,Q) and the filters (K,C,R,S); dw (K,C,R,S) = dL/dw from x and
+ * dy; db (K) = dL/dbias, the sum of dy over images and positions. Stride 1: dx is the forward
+ * implicit GEMM on the transposed, flipped filters (padding R-1-pad, S-1-pad), dw a tcgen05
+ * implicit GEMM over (image, position) split across the SMs and reduced in a fixed order;
+ * other strides and problems under 1e7 FLOP run direct FP32 kernels with the reference's loop
+ * order. db is a fixed-order reduction. precision as mfb_precision_t. Outputs are overwritten;
+ * n == 0 gives dw = 0, db = 0. */
+MFB_API mfb_status_t mfb_conv2d_bwd_data(int device, mfb_stream_t stream, int n, int c, int h, int w, int k, int r,
+                                         int s, int stride, int pad, const float* dy, const float* wgt, float* dx,
+                                         int precision);
+MFB_API mfb_status_t mfb_conv2d_bwd_filter(int device, mfb_stream_t stream, int n, int c, int h, int w, int k, int r,
+                                           int s, int stride, int pad, const float* x, const float* dy, float* dw,
+                                           int precision);
+MFB_API mfb_status_t mfb_conv2d_bwd_bias(int device, mfb_stream_t stream, int n, int k, int p, int q, const float* dy,
+                                         float* db);
 
 /* ---------------------------------------------------------------- covariance / correlation */
 /* cov (cols x cols, row stride ldcov) = X_c^T X_c / max(rows - 1, 1), X_c = X minus its column

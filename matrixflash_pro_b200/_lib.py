@@ -23,7 +23,7 @@ EXPORTED_SYMBOLS = (
     "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_set_sm_limit",
     "mfb_plan_tune", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
     "mfb_conv2d_fwd", "mfb_naive_sgemm", "mfb_probe_wait_timeout", "mfb_covariance", "mfb_correlation",
-    "mfb_probe_tf32_mma_tflops",
+    "mfb_probe_tf32_mma_tflops", "mfb_conv2d_bwd_data", "mfb_conv2d_bwd_filter", "mfb_conv2d_bwd_bias",
 )
 
 
@@ -64,6 +64,9 @@ def _declare(lib):
         "mfb_cuda_device_count": (st, [ctypes.POINTER(ctypes.c_int)]),
         "mfb_sgemm": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_sgemm_noalloc": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
+        "mfb_conv2d_bwd_data": (st, [ctypes.c_int, _vp] + [ctypes.c_int] * 9 + [_vp, _vp, _vp, ctypes.c_int]),
+        "mfb_conv2d_bwd_filter": (st, [ctypes.c_int, _vp] + [ctypes.c_int] * 9 + [_vp, _vp, _vp, ctypes.c_int]),
+        "mfb_conv2d_bwd_bias": (st, [ctypes.c_int, _vp] + [ctypes.c_int] * 4 + [_vp, _vp]),
         "mfb_probe_tf32_mma_tflops": (st, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float)]),
         "mfb_covariance": (st, [ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int,
                                 ctypes.c_int]),

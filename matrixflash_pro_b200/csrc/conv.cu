@@ -48,7 +48,7 @@ constexpr int kPackRows = 2;
 constexpr int kPackMaxWp = 512;  // padded width the shared tile holds; wider images use the generic kernel
 
 __global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __restrict__ x, int c, int h, int w,
-                                                             int pad, int cp, int hp, int wp, int vec,
+                                                             int pad_h, int pad_w, int cp, int hp, int wp, int vec,
                                                              float* __restrict__ hi, float* __restrict__ lo) {
     extern __shared__ float tile[];  // [32][stride], stride = kPackRows * wp rounded up to odd
     const int stride = (kPackRows * wp) | 1;
@@ -70,11 +70,11 @@ __global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __rest
             const int rem = i - cc * rows * w4;
             const int rr = rem / w4;
             const int q4 = rem - rr * w4;
-            const int ih = pr0 + rr - pad, ch = c0 + cc;
+            const int ih = pr0 + rr - pad_h, ch = c0 + cc;
             if (ih >= 0 && ih < h && ch < c) {
                 const float4 v = __ldg(reinterpret_cast<const float4*>(
                     x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + 4 * q4));
-                float* dst = tile + cc * stride + rr * wp + pad + 4 * q4;
+                float* dst = tile + cc * stride + rr * wp + pad_w + 4 * q4;
                 dst[0] = v.x;
                 dst[1] = v.y;
                 dst[2] = v.z;
@@ -87,9 +87,9 @@ __global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __rest
             const int rem = i - cc * rows * w;
             const int rr = rem / w;
             const int iw = rem - rr * w;
-            const int ih = pr0 + rr - pad, ch = c0 + cc;
+            const int ih = pr0 + rr - pad_h, ch = c0 + cc;
             if (ih >= 0 && ih < h && ch < c)
-                tile[cc * stride + rr * wp + pad + iw] =
+                tile[cc * stride + rr * wp + pad_w + iw] =
                     __ldg(x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + iw);
         }
     }
@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __rest
 // grid (ceil(Hp*Wp / 64), ceil(Cp / 32), N): a 32-channel x 64-position tile is read
 // along positions (coalesced in W) and written as 128-byte channel rows.
 __global__ void __launch_bounds__(256) conv_pack_input_kernel(const float* __restrict__ x, int c, int h, int w,
-                                                              int pad, int cp, int hp, int wp,
+                                                              int pad_h, int pad_w, int cp, int hp, int wp,
                                                               float* __restrict__ hi, float* __restrict__ lo) {
     __shared__ float tile[32][65];
     const int npos = hp * wp;
@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(256) conv_pack_input_kernel(const float* __res
         const int pos = pos0 + pp, ch = c0 + cc;
         float v = 0.0f;
         if (pos < npos && ch < c) {
-            const int ih = pos / wp - pad, iw = pos % wp - pad;
+            const int ih = pos / wp - pad_h, iw = pos % wp - pad_w;
             if (ih >= 0 && ih < h && iw >= 0 && iw < w)
                 v = __ldg(x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + iw);
         }
@@ -140,8 +140,10 @@ __global__ void __launch_bounds__(256) conv_pack_input_kernel(const float* __res
     }
 }
 
-// w (K,C,R,S) -> W [R*S][K][Cp].
-__global__ void conv_pack_weights_kernel(const float* __restrict__ wt, int kf, int c, int r, int s, int cp,
+// w (K,C,R,S) -> W [R*S][K][Cp]. flip != 0: `wt` is the (C,K,R,S) filter bank of the forward
+// conv whose input gradient is being formed; filter f, channel ch, tap (rr, ss) of the
+// packed bank is wt[ch][f][R-1-rr][S-1-ss] (the transposed, spatially flipped filters).
+__global__ void conv_pack_weights_kernel(const float* __restrict__ wt, int kf, int c, int r, int s, int cp, int flip,
                                          float* __restrict__ hi, float* __restrict__ lo) {
     const int groups = cp / 4;
     const long long total = static_cast<long long>(r) * s * kf * groups;
@@ -156,7 +158,12 @@ __global__ void conv_pack_weights_kernel(const float* __restrict__ wt, int kf, i
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int ch = 4 * g + i;
-            v[i] = ch < c ? __ldg(wt + ((static_cast<long long>(f) * c + ch) * r + rr) * s + ss) : 0.0f;
+            if (ch >= c)
+                v[i] = 0.0f;
+            else if (flip)
+                v[i] = __ldg(wt + ((static_cast<long long>(ch) * kf + f) * r + (r - 1 - rr)) * s + (s - 1 - ss));
+            else
+                v[i] = __ldg(wt + ((static_cast<long long>(f) * c + ch) * r + rr) * s + ss);
         }
         write_planes4(hi, lo, idx * 4, v[0], v[1], v[2], v[3]);
     }
@@ -212,6 +219,123 @@ mfb_status_t conv2d_direct(cudaStream_t stream, int n, int c, int h, int w, int 
     return MFB_OK;
 }
 
+// ------------------------------------------------------------------------------------ backward kernels
+
+// dy (N,K,P,Q) -> G [N][K][ldy]: output positions j = p*Wp + q of X's padded width, zeros for
+// q >= Q and j >= P*Wp; 4 positions per thread.
+__global__ void conv_pack_grad_kernel(const float* __restrict__ dy, int kf, int P, int Q, int wp, int ldy,
+                                      long long groups, float* __restrict__ hi, float* __restrict__ lo) {
+    const int per_row = ldy / 4;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < groups;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long row = idx / per_row;  // img * kf + f
+        const int j0 = static_cast<int>(idx - row * per_row) * 4;
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int j = j0 + e;
+            const int pr = j / wp, q = j - (j / wp) * wp;
+            v[e] = (pr < P && q < Q) ? __ldg(dy + (row * P + pr) * Q + q) : 0.0f;
+        }
+        write_planes4(hi, lo, row * ldy + j0, v[0], v[1], v[2], v[3]);
+    }
+}
+
+// dW[f][c][r][s] = sum over splits, in split order, of the partial tiles of the weight-gradient GEMM.
+__global__ void conv_wgrad_reduce_kernel(const float* __restrict__ partial, int splits, long long rows_alloc,
+                                         int ld_partial, int kf, int c, int taps, int cg, float* __restrict__ dw) {
+    const long long total = static_cast<long long>(kf) * c * taps;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int tap = static_cast<int>(idx % taps);
+        const long long rest = idx / taps;
+        const int ch = static_cast<int>(rest % c);
+        const int f = static_cast<int>(rest / c);
+        const long long m = static_cast<long long>(tap) * cg + ch;
+        float sum = 0.0f;
+        for (int sp = 0; sp < splits; ++sp) sum += partial[(sp * rows_alloc + m) * ld_partial + f];
+        dw[idx] = sum;
+    }
+}
+
+// Direct restatements of the reference's backward kernels (src/nn/backward/convolution_kernels.cuh:9-82),
+// one thread per output, FP32 FMA: other strides and problems too small for the tensor path.
+__global__ void conv_bwd_data_direct_kernel(const float* __restrict__ grad, const float* __restrict__ wt,
+                                            float* __restrict__ dx, int n, int c, int h, int w, int kf, int r, int s,
+                                            int P, int Q, int stride, int pad) {
+    const long long total = static_cast<long long>(n) * c * h * w;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int iw = static_cast<int>(idx % w);
+        const int ih = static_cast<int>((idx / w) % h);
+        const int ch = static_cast<int>((idx / (static_cast<long long>(w) * h)) % c);
+        const long long img = idx / (static_cast<long long>(c) * h * w);
+        float acc = 0.0f;
+        for (int f = 0; f < kf; ++f)
+            for (int kh = 0; kh < r; ++kh) {
+                const int ohl = ih + pad - kh;
+                if (ohl < 0 || ohl % stride != 0) continue;
+                const int oh = ohl / stride;
+                if (oh >= P) continue;
+                for (int kw = 0; kw < s; ++kw) {
+                    const int owl = iw + pad - kw;
+                    if (owl < 0 || owl % stride != 0) continue;
+                    const int ow = owl / stride;
+                    if (ow >= Q) continue;
+                    acc = fmaf(__ldg(grad + ((img * kf + f) * P + oh) * Q + ow),
+                               __ldg(wt + ((static_cast<long long>(f) * c + ch) * r + kh) * s + kw), acc);
+                }
+            }
+        dx[idx] = acc;
+    }
+}
+
+__global__ void conv_bwd_filter_direct_kernel(const float* __restrict__ grad, const float* __restrict__ x,
+                                              float* __restrict__ dw, int n, int c, int h, int w, int kf, int r,
+                                              int s, int P, int Q, int stride, int pad) {
+    const long long total = static_cast<long long>(kf) * c * r * s;
+    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int kw = static_cast<int>(idx % s);
+        const int kh = static_cast<int>((idx / s) % r);
+        const int ch = static_cast<int>((idx / (static_cast<long long>(s) * r)) % c);
+        const int f = static_cast<int>(idx / (static_cast<long long>(c) * r * s));
+        float acc = 0.0f;
+        for (int img = 0; img < n; ++img)
+            for (int oh = 0; oh < P; ++oh) {
+                const int ih = oh * stride + kh - pad;
+                if (ih < 0 || ih >= h) continue;
+                for (int ow = 0; ow < Q; ++ow) {
+                    const int iw = ow * stride + kw - pad;
+                    if (iw < 0 || iw >= w) continue;
+                    acc = fmaf(__ldg(grad + ((static_cast<long long>(img) * kf + f) * P + oh) * Q + ow),
+                               __ldg(x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + iw), acc);
+                }
+            }
+        dw[idx] = acc;
+    }
+}
+
+// dB[f] = sum over images and positions of dy[n][f]: one block per filter, per-thread partial
+// sums in a fixed stride pattern, then a fixed-order tree in shared memory (deterministic).
+__global__ void __launch_bounds__(256) conv_bwd_bias_kernel(const float* __restrict__ dy, int n, int kf,
+                                                            long long plane, float* __restrict__ db) {
+    __shared__ float part[256];
+    const int f = blockIdx.x;
+    float acc = 0.0f;
+    for (int img = 0; img < n; ++img) {
+        const float* src = dy + (static_cast<long long>(img) * kf + f) * plane;
+        for (long long j = threadIdx.x; j < plane; j += blockDim.x) acc += __ldg(src + j);
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    for (int width = 128; width > 0; width >>= 1) {
+        if (threadIdx.x < width) part[threadIdx.x] += part[threadIdx.x + width];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) db[f] = part[0];
+}
+
 // ------------------------------------------------------------------------------------ tcgen05 conv table
 struct ConvEntry {
     int bn, planes;
@@ -251,42 +375,68 @@ const ConvEntry* pick_conv(int kf, int planes) {
     return best;
 }
 
+template <int BN, int PLANES>
+ConvEntry make_wgrad_entry() {
+    using P = ConvWgradProblem<BN, PLANES>;
+    using L = TcLayout<P>;
+    return ConvEntry{BN, PLANES, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes, L::kThreads};
+}
+
+const ConvEntry* wgrad_table(int* count) {
+    static const ConvEntry table[] = {
+        make_wgrad_entry<64, 2>(), make_wgrad_entry<128, 2>(), make_wgrad_entry<256, 2>(),
+        make_wgrad_entry<64, 1>(), make_wgrad_entry<128, 1>(), make_wgrad_entry<256, 1>(),
+    };
+    *count = static_cast<int>(sizeof(table) / sizeof(table[0]));
+    return table;
+}
+
+// Narrowest filter tile covering K (64, 128 or 256 filters), else 256-filter tiles.
+const ConvEntry* pick_wgrad(int kf, int planes) {
+    int count = 0;
+    const ConvEntry* t = wgrad_table(&count);
+    const ConvEntry* best = nullptr;
+    for (int i = 0; i < count; ++i)
+        if (t[i].planes == planes && t[i].bn >= kf && (!best || t[i].bn < best->bn)) best = &t[i];
+    if (!best)
+        for (int i = 0; i < count; ++i)
+            if (t[i].planes == planes && (!best || t[i].bn > best->bn)) best = &t[i];
+    return best;
+}
+
 long long round_up64(long long v) { return (v + 63) / 64 * 64; }
 
 }  // namespace
 
-size_t conv2d_workspace_bytes(int n, int c, int h, int w, int k, int r, int s, int stride, int pad, int precision) {
-    if (stride != 1) return 0;
+struct ConvGeom {
+    int n, c, h, w, k, r, s, pad_h, pad_w;
+};
+
+size_t conv_tc_workspace_bytes(const ConvGeom& g, int precision) {
     const long long planes = precision == MFB_PRECISION_FP32 ? 2 : 1;
-    const long long cp = (c + 3) / 4 * 4;
-    const long long a = round_up64(static_cast<long long>(n) * (h + 2 * pad) * (w + 2 * pad) * cp);
-    const long long b = round_up64(static_cast<long long>(r) * s * k * cp);
+    const long long cp = (g.c + 3) / 4 * 4;
+    const long long a = round_up64(static_cast<long long>(g.n) * (g.h + 2 * g.pad_h) * (g.w + 2 * g.pad_w) * cp);
+    const long long b = round_up64(static_cast<long long>(g.r) * g.s * g.k * cp);
     return static_cast<size_t>(planes * (a + b) * 4);
 }
 
-mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
-                           int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
-                           int precision) {
-    const int P = (h + 2 * pad - r) / stride + 1;
-    const int Q = (w + 2 * pad - s) / stride + 1;
-    if (n == 0 || P <= 0 || Q <= 0) return MFB_OK;
-    // Other strides, and problems too small to amortize the tensor path's three launches and
-    // pipeline fill (~25 us; e.g. 8x3x32x32 with 16 filters, 7 MFLOP): the direct kernel,
-    // one launch, FP32 FMA chains in the reference's order (at least as accurate as either
-    // precision policy asks).
-    const double flops = 2.0 * n * k * P * Q * static_cast<double>(c) * r * s;
-    if (stride != 1 || flops < kConvDirectMaxFlops)
-        return conv2d_direct(stream, n, c, h, w, k, r, s, stride, pad, P, Q, x, wgt, bias, y);
-
+// Stride-1 implicit GEMM on tcgen05: y (N,K,P,Q) = bias + x (N,C,H,W) correlated with the filter
+// bank, P = H + 2 pad_h - R + 1, Q = W + 2 pad_w - S + 1. flip selects the packing of `wgt`
+// (conv_pack_weights_kernel); bias may be null.
+mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g, const float* x, const float* wgt,
+                             int flip, const float* bias, float* y, int precision) {
+    const int n = g.n, c = g.c, h = g.h, w = g.w, k = g.k, r = g.r, s = g.s;
+    const int P = h + 2 * g.pad_h - r + 1;
+    const int Q = w + 2 * g.pad_w - s + 1;
     const int planes = precision == MFB_PRECISION_FP32 ? 2 : 1;
     const int cp = (c + 3) / 4 * 4;
-    const int hp = h + 2 * pad, wp = w + 2 * pad;
+    const int hp = h + 2 * g.pad_h, wp = w + 2 * g.pad_w;
     const long long npos = static_cast<long long>(hp) * wp;
     if (n > 65535 || npos > 0x7fffffffLL) return fail(MFB_EUNSUPPORTED, "conv2d input too large");
     const ConvEntry* e = pick_conv(k, planes);
     if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 conv configuration");
 
-    const size_t need = conv2d_workspace_bytes(n, c, h, w, k, r, s, stride, pad, precision);
+    const size_t need = conv_tc_workspace_bytes(g, precision);
     void* ws = nullptr;
     MFB_TRY(stream_workspace(device, stream, need, &ws));
     const long long a_plane = round_up64(static_cast<long long>(n) * npos * cp);
@@ -295,7 +445,6 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
     float* a_lo = planes == 2 ? a_hi + a_plane : nullptr;
     float* b_hi = a_hi + planes * a_plane;
     float* b_lo = planes == 2 ? b_hi + b_plane : nullptr;
-
     if (wp <= kPackMaxWp) {
         const size_t tile_bytes = static_cast<size_t>(32) * ((kPackRows * wp) | 1) * 4;
         if (tile_bytes > 48 * 1024)
@@ -305,15 +454,16 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
                          "conv prepass smem attribute");
         const int vec = (w % 4 == 0 && aligned16(x)) ? 1 : 0;
         dim3 pgrid(static_cast<unsigned>((hp + kPackRows - 1) / kPackRows), static_cast<unsigned>((cp + 31) / 32), n);
-        conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, pad, cp, hp, wp, vec, a_hi, a_lo);
+        conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, g.pad_h, g.pad_w, cp, hp, wp, vec,
+                                                                 a_hi, a_lo);
     } else {
         dim3 pgrid(static_cast<unsigned>((npos + 63) / 64), static_cast<unsigned>((cp + 31) / 32), n);
-        conv_pack_input_kernel<<<pgrid, 256, 0, stream>>>(x, c, h, w, pad, cp, hp, wp, a_hi, a_lo);
+        conv_pack_input_kernel<<<pgrid, 256, 0, stream>>>(x, c, h, w, g.pad_h, g.pad_w, cp, hp, wp, a_hi, a_lo);
     }
     MFB_CUDA_TRY(cudaGetLastError(), "conv input prepass launch");
     const long long wgroups = static_cast<long long>(r) * s * k * (cp / 4);
     conv_pack_weights_kernel<<<static_cast<int>(std::min<long long>((wgroups + 255) / 256, 148LL * 4)), 256, 0,
-                               stream>>>(wgt, k, c, r, s, cp, b_hi, b_lo);
+                               stream>>>(wgt, k, c, r, s, cp, flip, b_hi, b_lo);
     MFB_CUDA_TRY(cudaGetLastError(), "conv weight prepass launch");
 
     // X: dims (Cp, Hp*Wp, N, planes); W: dims (Cp, K, R*S, planes); boxes of 32 channels.
@@ -343,7 +493,7 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
     p.kf = k;
     p.r = r;
     p.s = s;
-    p.pad = pad;
+    p.pad = g.pad_h;
     p.hp = hp;
     p.wp = wp;
     p.p_out = P;
@@ -367,6 +517,176 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
     void* args[] = {&map_a, &map_b, &p};
     MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(grid), dim3(e->threads), args, static_cast<size_t>(e->smem), stream),
                  "tcgen05 conv launch");
+    return MFB_OK;
+}
+
+
+size_t conv2d_workspace_bytes(int n, int c, int h, int w, int k, int r, int s, int stride, int pad, int precision) {
+    if (stride != 1) return 0;
+    return conv_tc_workspace_bytes(ConvGeom{n, c, h, w, k, r, s, pad, pad}, precision);
+}
+
+mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
+                           int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
+                           int precision) {
+    const int P = (h + 2 * pad - r) / stride + 1;
+    const int Q = (w + 2 * pad - s) / stride + 1;
+    if (n == 0 || P <= 0 || Q <= 0) return MFB_OK;
+    // Other strides, and problems too small to amortize the tensor path's three launches and
+    // pipeline fill (~25 us; e.g. 8x3x32x32 with 16 filters, 7 MFLOP): the direct kernel,
+    // one launch, FP32 FMA chains in the reference's order (at least as accurate as either
+    // precision policy asks).
+    const double flops = 2.0 * n * k * P * Q * static_cast<double>(c) * r * s;
+    if (stride != 1 || flops < kConvDirectMaxFlops)
+        return conv2d_direct(stream, n, c, h, w, k, r, s, stride, pad, P, Q, x, wgt, bias, y);
+    return conv_tc_forward(device, stream, ConvGeom{n, c, h, w, k, r, s, pad, pad}, x, wgt, 0, bias, y, precision);
+}
+
+mfb_status_t conv2d_bwd_data_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
+                                    int stride, int pad, const float* dy, const float* wgt, float* dx,
+                                    int precision) {
+    const int P = (h + 2 * pad - r) / stride + 1;
+    const int Q = (w + 2 * pad - s) / stride + 1;
+    if (n == 0) return MFB_OK;
+    const double flops = 2.0 * n * k * P * Q * static_cast<double>(c) * r * s;
+    // Stride 1: dX is the forward correlation of dY (K channels, P x Q) with the transposed,
+    // flipped filters and padding (R-1-pad, S-1-pad): P + R - 1 - 2 pad = H rows out.
+    if (stride == 1 && pad <= r - 1 && pad <= s - 1 && flops >= kConvDirectMaxFlops)
+        return conv_tc_forward(device, stream, ConvGeom{n, k, P, Q, c, r, s, r - 1 - pad, s - 1 - pad}, dy, wgt, 1,
+                               nullptr, dx, precision);
+    const long long total = static_cast<long long>(n) * c * h * w;
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    conv_bwd_data_direct_kernel<<<blocks, 256, 0, stream>>>(dy, wgt, dx, n, c, h, w, k, r, s, P, Q, stride, pad);
+    MFB_CUDA_TRY(cudaGetLastError(), "conv2d input-gradient launch");
+    return MFB_OK;
+}
+
+mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r,
+                                      int s, int stride, int pad, const float* x, const float* dy, float* dw,
+                                      int precision) {
+    const int P = (h + 2 * pad - r) / stride + 1;
+    const int Q = (w + 2 * pad - s) / stride + 1;
+    const long long wtotal = static_cast<long long>(k) * c * r * s;
+    const double flops = 2.0 * n * k * P * Q * static_cast<double>(c) * r * s;
+    if (n == 0) {  // an empty batch contributes nothing: dW = 0
+        MFB_CUDA_TRY(cudaMemsetAsync(dw, 0, static_cast<size_t>(wtotal) * 4, stream), "dW clear");
+        return MFB_OK;
+    }
+    const int planes = precision == MFB_PRECISION_FP32 ? 2 : 1;
+    const int hp = h + 2 * pad, wp = w + 2 * pad;
+    const long long npos = static_cast<long long>(hp) * wp;
+    const long long gpos = static_cast<long long>(P) * wp;
+    const ConvEntry* e = pick_wgrad(k, planes);
+    const bool tensor = stride == 1 && flops >= kConvDirectMaxFlops && e != nullptr && n <= 65535 &&
+                        npos <= 0x7fffffffLL && gpos <= 0x7fffffffLL;
+    if (!tensor) {
+        const int blocks = static_cast<int>(std::min<long long>((wtotal + 127) / 128, 148LL * 16));
+        conv_bwd_filter_direct_kernel<<<blocks, 128, 0, stream>>>(dy, x, dw, n, c, h, w, k, r, s, P, Q, stride, pad);
+        MFB_CUDA_TRY(cudaGetLastError(), "conv2d weight-gradient launch");
+        return MFB_OK;
+    }
+    const int cp = (c + 3) / 4 * 4;
+    const int cg = (c + 31) / 32 * 32;
+    const int ldy = static_cast<int>((gpos + 3) / 4 * 4);
+    ConvWgradParams p{};
+    p.n_img = n;
+    p.c = c;
+    p.kf = k;
+    p.r = r;
+    p.s = s;
+    p.cg = cg;
+    p.wp = wp;
+    p.kb_per_img = static_cast<int>((gpos + 31) / 32);
+    p.rows_total = r * s * cg;
+    p.tiles_m = (p.rows_total + kTcBM - 1) / kTcBM;
+    p.tiles_f = (k + e->bn - 1) / e->bn;
+    p.ld_partial = p.tiles_f * e->bn;
+    const long long total_kb = static_cast<long long>(n) * p.kb_per_img;
+    // About two work units per SM, each at least 16 K blocks long.
+    const int sms = sm_count(device);
+    long long splits = (2LL * sms + p.tiles_m * p.tiles_f - 1) / (p.tiles_m * p.tiles_f);
+    splits = std::max(1LL, std::min(splits, total_kb / 16));
+    const long long kbs = (total_kb + splits - 1) / splits;
+    splits = (total_kb + kbs - 1) / kbs;
+    p.kb_per_split = static_cast<int>(kbs);
+    p.splits = static_cast<int>(splits);
+    p.wait_limit_ns = wait_limit_ns();
+    const long long rows_alloc = static_cast<long long>(p.tiles_m) * kTcBM;
+
+    const long long a_plane = round_up64(static_cast<long long>(n) * npos * cp);
+    const long long g_plane = round_up64(static_cast<long long>(n) * k * ldy);
+    const long long part = round_up64(splits * rows_alloc * p.ld_partial);
+    const size_t need = static_cast<size_t>((planes * (a_plane + g_plane) + part) * 4);
+    void* ws = nullptr;
+    MFB_TRY(stream_workspace(device, stream, need, &ws));
+    float* a_hi = static_cast<float*>(ws);
+    float* a_lo = planes == 2 ? a_hi + a_plane : nullptr;
+    float* g_hi = a_hi + planes * a_plane;
+    float* g_lo = planes == 2 ? g_hi + g_plane : nullptr;
+    p.partial = g_hi + planes * g_plane;
+
+    // X planes (as the forward), dY planes in X's padded width.
+    if (wp <= kPackMaxWp) {
+        const size_t tile_bytes = static_cast<size_t>(32) * ((kPackRows * wp) | 1) * 4;
+        if (tile_bytes > 48 * 1024)
+            MFB_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(&conv_pack_rows_kernel),
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(tile_bytes)),
+                         "conv prepass smem attribute");
+        const int vec = (w % 4 == 0 && aligned16(x)) ? 1 : 0;
+        dim3 pgrid(static_cast<unsigned>((hp + kPackRows - 1) / kPackRows), static_cast<unsigned>((cp + 31) / 32), n);
+        conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, pad, pad, cp, hp, wp, vec, a_hi, a_lo);
+    } else {
+        dim3 pgrid(static_cast<unsigned>((npos + 63) / 64), static_cast<unsigned>((cp + 31) / 32), n);
+        conv_pack_input_kernel<<<pgrid, 256, 0, stream>>>(x, c, h, w, pad, pad, cp, hp, wp, a_hi, a_lo);
+    }
+    MFB_CUDA_TRY(cudaGetLastError(), "wgrad input prepass launch");
+    const long long groups = static_cast<long long>(n) * k * (ldy / 4);
+    conv_pack_grad_kernel<<<static_cast<int>(std::min<long long>((groups + 255) / 256, 148LL * 8)), 256, 0, stream>>>(
+        dy, k, P, Q, wp, ldy, groups, g_hi, g_lo);
+    MFB_CUDA_TRY(cudaGetLastError(), "wgrad gradient prepass launch");
+
+    CUtensorMap map_a, map_b;
+    {
+        // X planes read MN-major: channels innermost, 32-channel x 32-position boxes.
+        const uint64_t dims[4] = {static_cast<uint64_t>(cp), static_cast<uint64_t>(npos), static_cast<uint64_t>(n),
+                                  static_cast<uint64_t>(planes)};
+        const uint64_t strides[3] = {static_cast<uint64_t>(cp) * 4, static_cast<uint64_t>(npos) * cp * 4,
+                                     static_cast<uint64_t>(a_plane) * 4};
+        const uint32_t box[4] = {32, 32, 1, static_cast<uint32_t>(planes)};
+        MFB_TRY(encode_tensor_map(&map_a, a_hi, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B));
+    }
+    {
+        const uint64_t dims[4] = {static_cast<uint64_t>(gpos), static_cast<uint64_t>(k), static_cast<uint64_t>(n),
+                                  static_cast<uint64_t>(planes)};
+        const uint64_t strides[3] = {static_cast<uint64_t>(ldy) * 4, static_cast<uint64_t>(k) * ldy * 4,
+                                     static_cast<uint64_t>(g_plane) * 4};
+        const uint32_t box[4] = {32, static_cast<uint32_t>(e->bn), 1, static_cast<uint32_t>(planes)};
+        MFB_TRY(encode_tensor_map(&map_b, g_hi, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B));
+    }
+    const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_f * p.splits;
+    if (tiles > 0x7fffffffLL) return fail(MFB_EINVAL, "weight gradient has too many work units");
+    static std::mutex attr_mutex;
+    {
+        std::lock_guard<std::mutex> lock(attr_mutex);
+        MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem),
+                     "wgrad smem attribute");
+    }
+    void* args[] = {&map_a, &map_b, &p};
+    const int grid = static_cast<int>(std::min<long long>(tiles, sms));
+    MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(grid), dim3(e->threads), args, static_cast<size_t>(e->smem), stream),
+                 "tcgen05 weight-gradient launch");
+    const int rblocks = static_cast<int>(std::min<long long>((wtotal + 255) / 256, 148LL * 8));
+    conv_wgrad_reduce_kernel<<<rblocks, 256, 0, stream>>>(p.partial, p.splits, rows_alloc, p.ld_partial, k, c, r * s,
+                                                          cg, dw);
+    MFB_CUDA_TRY(cudaGetLastError(), "wgrad reduce launch");
+    return MFB_OK;
+}
+
+mfb_status_t conv2d_bwd_bias_launch(cudaStream_t stream, int n, int k, int P, int Q, const float* dy, float* db) {
+    if (k == 0) return MFB_OK;
+    conv_bwd_bias_kernel<<<k, 256, 0, stream>>>(dy, n, k, static_cast<long long>(P) * Q, db);
+    MFB_CUDA_TRY(cudaGetLastError(), "conv2d bias-gradient launch");
     return MFB_OK;
 }
 

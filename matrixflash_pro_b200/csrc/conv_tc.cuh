@@ -95,8 +95,96 @@ struct ConvProblem {
 #pragma unroll
         for (int e = 0; e < COUNT; ++e) {
             const int f = t.f0 + col0_in_tile + e;
-            if (f < p.kf) base[f * plane] = v[e] + p.bias[f];
+            if (f < p.kf) base[f * plane] = p.bias ? v[e] + p.bias[f] : v[e];
         }
+    }
+};
+
+// ------------------------------------------------------------------------------------
+// Weight gradient, stride 1: dW[f][c][r][s] = sum_{n,p,q} dY[n][f][p][q] * Xpad[n][c][p+r][q+s].
+//
+// GEMM view: D[m][f] with m = tap * Cg + c (Cg = C rounded up to 32; rows of one 32-row
+// group share a tap), reduced over K = (image, output position j = p*Wp + q in the
+// padded-width space of X). A = X planes [n][Hp*Wp][Cp] read MN-major (channels
+// contiguous): the 32-channel x 32-position box of row group g sits at position
+// j0 + r*Wp + s of its tap. B = dY planes [n][K][P*Wp] (zeros for q >= Q) read K-major.
+// K is cut into `splits` equal ranges, one per output-tile work unit; each unit writes
+// its 128 x BN partial tile and conv_wgrad_reduce_kernel sums the splits in order.
+// K blocks past the last image read the maps' zero fill.
+// ------------------------------------------------------------------------------------
+struct ConvWgradParams {
+    int n_img, c, kf, r, s;
+    int cg;              // C rounded up to 32
+    int wp;              // padded width of X (output positions live in this width)
+    int kb_per_img;      // ceil(P * Wp / 32)
+    int kb_per_split;
+    int splits;
+    int tiles_m, tiles_f;
+    int rows_total;      // r * s * cg
+    int ld_partial;      // tiles_f * BN
+    float* partial;      // [splits][rows_total rounded up to 128][ld_partial]
+    unsigned long long wait_limit_ns;
+};
+
+template <int BN_, int PLANES_>
+struct ConvWgradProblem {
+    using Params = ConvWgradParams;
+    static constexpr int BN = BN_, PLANES = PLANES_, A_MN = 1, B_MN = 0;
+    static constexpr bool kStackB = PLANES_ == 2 && BN_ <= 64;  // dY tiles are K-major: hi, lo rows adjacent
+    static constexpr int kATileBytes = PLANES * kTcBM * 128;
+    static constexpr int kBTileBytes = PLANES * BN * 128;
+    static constexpr int STAGES = (196608 / (kATileBytes + kBTileBytes)) > 8 ? 8 : (196608 / (kATileBytes + kBTileBytes));
+    static constexpr int kKSteps = 4;
+    static_assert(STAGES >= 2, "wgrad tile configuration");
+
+    struct Tile {
+        int m0, f0, split;
+    };
+
+    __device__ static int num_tiles(const Params& p) { return p.tiles_m * p.tiles_f * p.splits; }
+    __device__ static int num_kb(const Params& p) { return p.kb_per_split; }
+
+    __device__ static Tile tile(const Params& p, int t) {
+        const int split = t / (p.tiles_m * p.tiles_f);
+        const int rest = t - split * p.tiles_m * p.tiles_f;
+        return Tile{(rest / p.tiles_f) * kTcBM, (rest % p.tiles_f) * BN, split};
+    }
+
+    __device__ static int valid_cols(const Params& p, const Tile& t) { return min(BN, p.kf - t.f0); }
+
+    __device__ static void load(const Params& p, const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile,
+                                uint8_t* b_tile, uint64_t* bar, const Tile& t, int kb) {
+        const long long kg = static_cast<long long>(t.split) * p.kb_per_split + kb;
+        const int img = static_cast<int>(kg / p.kb_per_img);
+        const int j0 = static_cast<int>(kg - static_cast<long long>(img) * p.kb_per_img) * 32;
+#pragma unroll
+        for (int g = 0; g < kTcBM / 32; ++g) {
+            const int m = t.m0 + 32 * g;
+            const int tap = m / p.cg;
+            // rows past the last tap read channel coordinates beyond the map: zeros
+            const int c0 = tap < p.r * p.s ? m - tap * p.cg : p.cg;
+            const int rr = tap < p.r * p.s ? tap / p.s : 0;
+            const int shift = tap < p.r * p.s ? rr * p.wp + (tap - rr * p.s) : 0;
+            tma_load_4d(a_tile + g * PLANES * 4096, ta, bar, c0, j0 + shift, img, 0);
+        }
+        tma_load_4d(b_tile, tb, bar, j0, t.f0, img, 0);
+    }
+
+    // A: [group of 32 M][plane][32 K rows][32 M] (128B swizzle, 32-byte atoms); B: [plane][BN][32 K].
+    __device__ static uint64_t a_desc(uint32_t addr, int pl, int ks) {
+        return umma_smem_desc(addr + pl * 4096 + ks * 1024, PLANES * 4096, 512, kLayoutSwizzle128B_Base32B);
+    }
+    __device__ static uint64_t b_desc(uint32_t addr, int pl, int ks) {
+        return umma_smem_desc(addr + pl * BN * 128 + ks * 32, 16, 1024, kLayoutSwizzle128B);
+    }
+
+    template <int COUNT>
+    __device__ static void store(const Params& p, const Tile& t, int row_in_tile, int col0_in_tile, const float* v) {
+        const long long rows_alloc = static_cast<long long>(p.tiles_m) * kTcBM;
+        float* dst = p.partial + (static_cast<long long>(t.split) * rows_alloc + t.m0 + row_in_tile) * p.ld_partial +
+                     t.f0 + col0_in_tile;
+#pragma unroll
+        for (int e = 0; e < COUNT; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
     }
 };
 

@@ -616,4 +616,53 @@ MFB_API mfb_status_t mfb_conv2d_fwd(int device, mfb_stream_t stream_h, int n, in
                          bias, y, precision);
 }
 
+namespace {
+// Shape checks of the reference's validate_conv (src/nn/backward/convolution_kernels.cuh:98-115).
+mfb_status_t validate_conv_bwd(int n, int c, int h, int w, int k, int r, int s, int stride, int pad, int precision) {
+    if (n < 0 || c <= 0 || h <= 0 || w <= 0 || k <= 0 || r <= 0 || s <= 0 || pad < 0)
+        return fail(MFB_EINVAL, "conv2d backward expects positive C, H, W, K, R, S and non-negative N and padding");
+    if (stride <= 0) return fail(MFB_EINVAL, "conv2d backward stride must be positive");
+    if (h + 2 * pad < r || w + 2 * pad < s) return fail(MFB_ESHAPE, "conv2d backward shape mismatch");
+    if (precision != MFB_PRECISION_FP32 && precision != MFB_PRECISION_TF32)
+        return fail(MFB_EINVAL, "Invalid conv precision policy");
+    return MFB_OK;
+}
+}  // namespace
+
+MFB_API mfb_status_t mfb_conv2d_bwd_data(int device, mfb_stream_t stream_h, int n, int c, int h, int w, int k, int r,
+                                         int s, int stride, int pad, const float* dy, const float* wgt, float* dx,
+                                         int precision) {
+    clear_error();
+    MFB_TRY(validate_conv_bwd(n, c, h, w, k, r, s, stride, pad, precision));
+    if (n > 0 && (!dy || !wgt || !dx)) return fail(MFB_EINVAL, "null conv2d backward pointer");
+    if (n > 0 && (dx == dy || dx == wgt)) return fail(MFB_EINVAL, "conv2d input gradient cannot alias an input");
+    DeviceGuard guard;
+    MFB_TRY(select_device(device));
+    return conv2d_bwd_data_launch(device, reinterpret_cast<cudaStream_t>(stream_h), n, c, h, w, k, r, s, stride, pad,
+                                  dy, wgt, dx, precision);
+}
+
+MFB_API mfb_status_t mfb_conv2d_bwd_filter(int device, mfb_stream_t stream_h, int n, int c, int h, int w, int k,
+                                           int r, int s, int stride, int pad, const float* x, const float* dy,
+                                           float* dw, int precision) {
+    clear_error();
+    MFB_TRY(validate_conv_bwd(n, c, h, w, k, r, s, stride, pad, precision));
+    if (!dw || (n > 0 && (!x || !dy))) return fail(MFB_EINVAL, "null conv2d backward pointer");
+    if (dw == x || dw == dy) return fail(MFB_EINVAL, "conv2d weight gradient cannot alias an input");
+    DeviceGuard guard;
+    MFB_TRY(select_device(device));
+    return conv2d_bwd_filter_launch(device, reinterpret_cast<cudaStream_t>(stream_h), n, c, h, w, k, r, s, stride, pad,
+                                    x, dy, dw, precision);
+}
+
+MFB_API mfb_status_t mfb_conv2d_bwd_bias(int device, mfb_stream_t stream_h, int n, int k, int p, int q,
+                                         const float* dy, float* db) {
+    clear_error();
+    if (n < 0 || k < 0 || p < 0 || q < 0) return fail(MFB_EINVAL, "conv2d bias backward expects a rank-4 gradient");
+    if (k > 0 && (!db || (n > 0 && p > 0 && q > 0 && !dy))) return fail(MFB_EINVAL, "null conv2d backward pointer");
+    DeviceGuard guard;
+    MFB_TRY(select_device(device));
+    return conv2d_bwd_bias_launch(reinterpret_cast<cudaStream_t>(stream_h), n, k, p, q, dy, db);
+}
+
 }  // extern "C"

@@ -111,6 +111,13 @@ mfb_status_t gemv_launch(const mfb_gemm_desc& d, cudaStream_t stream, const floa
                          const float* bias, void* workspace, size_t workspace_bytes);
 
 // ---------------------------------------------------------------------- conv
+// conv2d backward (conv.cu): input gradient, weight gradient, bias gradient.
+mfb_status_t conv2d_bwd_data_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
+                                    int stride, int pad, const float* dy, const float* wgt, float* dx, int precision);
+mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r,
+                                      int s, int stride, int pad, const float* x, const float* dy, float* dw,
+                                      int precision);
+mfb_status_t conv2d_bwd_bias_launch(cudaStream_t stream, int n, int k, int P, int Q, const float* dy, float* db);
 mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
                            int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
                            int precision);

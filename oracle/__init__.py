@@ -5,7 +5,8 @@ CPU checkers for the dense FP32 contraction path:
 * ``libmfb_oracle.so`` — a C restatement (``oracle/mfb_oracle.c``) of the
   reference's ``gemm_f32`` arithmetic (src/hw/gemm_avx2.cpp:75-451), of
   ``gemm_reference`` (src/hw/gemm_scalar.cpp:12-33), of ``conv2d_kernel``
-  (src/nn/conv.cu:22-49) and of the column-bias epilogue
+  (src/nn/conv.cu:22-49), of the three conv2d backward kernels
+  (src/nn/backward/convolution_kernels.cuh:9-95) and of the column-bias epilogue
   (src/ops/gemm/gemm_fused.cu:23-40), plus FP64 references.
 * ``_ref/libmfref_cpu.so`` — the reference's own ``gemm_f32`` compiled from its
   sources by ``oracle/Makefile`` (present wherever that build ran).
@@ -66,6 +67,11 @@ def _restatement():
         lib.oracle_conv2d_f32.argtypes = conv_sig + [_f32p]
         lib.oracle_conv2d_f64.argtypes = conv_sig + [_f64p]
         lib.oracle_epilogue_f32.argtypes = [_f32p, ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        bwd_sig = [ctypes.c_int] * 9 + [_f32p, _f32p]
+        for suffix, outp in (("f32", _f32p), ("f64", _f64p)):
+            getattr(lib, f"oracle_conv2d_input_backward_{suffix}").argtypes = bwd_sig + [outp]
+            getattr(lib, f"oracle_conv2d_weight_backward_{suffix}").argtypes = bwd_sig + [outp]
+            getattr(lib, f"oracle_conv2d_bias_backward_{suffix}").argtypes = [ctypes.c_int] * 4 + [_f32p, outp]
         _rest = lib
     return _rest
 
@@ -195,6 +201,47 @@ def conv2d_f64(x, w, bias, stride=1, padding=0):
     y = np.zeros((n, k, p, q), dtype=np.float64)
     _restatement().oracle_conv2d_f64(n, c, h, wd, k, r, s, stride, padding, _p32(x), _p32(w), _p32(bias), _p64(y))
     return y
+
+
+def _bwd_shapes(grad, x_shape, w_shape, stride, padding):
+    n, c, h, wd = x_shape
+    k, c2, r, s = w_shape
+    p = (h + 2 * padding - r) // stride + 1
+    q = (wd + 2 * padding - s) // stride + 1
+    assert c == c2 and tuple(grad.shape) == (n, k, p, q), "conv2d backward shape mismatch"
+    return n, c, h, wd, k, r, s
+
+
+def conv2d_input_backward(grad, w, x_shape, stride=1, padding=0, f64=False):
+    """dL/dinput with the arithmetic of conv2d_input_backward_kernel (convolution_kernels.cuh:9-47)."""
+    grad = np.ascontiguousarray(grad, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, c, h, wd, k, r, s = _bwd_shapes(grad, x_shape, w.shape, stride, padding)
+    out = np.zeros((n, c, h, wd), dtype=np.float64 if f64 else np.float32)
+    fn = _restatement().oracle_conv2d_input_backward_f64 if f64 else _restatement().oracle_conv2d_input_backward_f32
+    fn(n, c, h, wd, k, r, s, stride, padding, _p32(grad), _p32(w), _p64(out) if f64 else _p32(out))
+    return out
+
+
+def conv2d_weight_backward(grad, x, w_shape, stride=1, padding=0, f64=False):
+    """dL/dweights with the arithmetic of conv2d_weight_backward_kernel (convolution_kernels.cuh:50-82)."""
+    grad = np.ascontiguousarray(grad, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, c, h, wd, k, r, s = _bwd_shapes(grad, x.shape, w_shape, stride, padding)
+    out = np.zeros((k, c, r, s), dtype=np.float64 if f64 else np.float32)
+    fn = _restatement().oracle_conv2d_weight_backward_f64 if f64 else _restatement().oracle_conv2d_weight_backward_f32
+    fn(n, c, h, wd, k, r, s, stride, padding, _p32(grad), _p32(x), _p64(out) if f64 else _p32(out))
+    return out
+
+
+def conv2d_bias_backward(grad, f64=False):
+    """dL/dbias with the arithmetic of conv2d_bias_backward_kernel (convolution_kernels.cuh:85-95)."""
+    grad = np.ascontiguousarray(grad, dtype=np.float32)
+    n, k, p, q = grad.shape
+    out = np.zeros(k, dtype=np.float64 if f64 else np.float32)
+    fn = _restatement().oracle_conv2d_bias_backward_f64 if f64 else _restatement().oracle_conv2d_bias_backward_f32
+    fn(n, k, p, q, _p32(grad), _p64(out) if f64 else _p32(out))
+    return out
 
 
 def col_mean_f32(x):

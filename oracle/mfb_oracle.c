@@ -213,6 +213,85 @@ ORACLE_API void oracle_conv2d_f64(int batch, int channels, int height, int width
 }
 
 /*
+ * conv2d backward, restated from the reference's kernels (src/nn/backward/convolution_kernels.cuh):
+ * conv2d_input_backward_kernel (:9-47), conv2d_weight_backward_kernel (:50-82) and
+ * conv2d_bias_backward_kernel (:85-95), same loop orders and skip rules. The products accumulate
+ * as `acc += a * b`, which nvcc contracts to one FMA; the bias sum is a plain add.
+ * ACC is float (FMA) or double (exact products) below.
+ */
+#define ORACLE_CONV_BWD(NAME, ACC, MAC)                                                                        \
+    ORACLE_API void oracle_conv2d_input_backward_##NAME(                                                      \
+        int batch, int channels, int height, int width, int filters, int kh_size, int kw_size, int stride,    \
+        int padding, const float* grad, const float* weights, ACC* input_grad) {                              \
+        const long out_h = (height + 2 * padding - kh_size) / stride + 1;                                    \
+        const long out_w = (width + 2 * padding - kw_size) / stride + 1;                                     \
+        for (int n = 0; n < batch; ++n)                                                                        \
+            for (int c = 0; c < channels; ++c)                                                                 \
+                for (int ih = 0; ih < height; ++ih)                                                            \
+                    for (int iw = 0; iw < width; ++iw) {                                                       \
+                        ACC acc = 0;                                                                           \
+                        for (int f = 0; f < filters; ++f)                                                      \
+                            for (int kh = 0; kh < kh_size; ++kh) {                                             \
+                                const long ohl = (long)ih + padding - kh;                                      \
+                                if (ohl < 0 || ohl % stride != 0) continue;                                    \
+                                const long oh = ohl / stride;                                                  \
+                                if (oh >= out_h) continue;                                                     \
+                                for (int kw = 0; kw < kw_size; ++kw) {                                         \
+                                    const long owl = (long)iw + padding - kw;                                  \
+                                    if (owl < 0 || owl % stride != 0) continue;                                \
+                                    const long ow = owl / stride;                                              \
+                                    if (ow >= out_w) continue;                                                 \
+                                    const float g = grad[(((size_t)n * filters + f) * out_h + oh) * out_w + ow]; \
+                                    const float w = weights[(((size_t)f * channels + c) * kh_size + kh) * kw_size + kw]; \
+                                    acc = MAC(g, w, acc);                                                      \
+                                }                                                                              \
+                            }                                                                                  \
+                        input_grad[(((size_t)n * channels + c) * height + ih) * width + iw] = acc;             \
+                    }                                                                                          \
+    }                                                                                                          \
+    ORACLE_API void oracle_conv2d_weight_backward_##NAME(                                                     \
+        int batch, int channels, int height, int width, int filters, int kh_size, int kw_size, int stride,    \
+        int padding, const float* grad, const float* input, ACC* weight_grad) {                               \
+        const long out_h = (height + 2 * padding - kh_size) / stride + 1;                                    \
+        const long out_w = (width + 2 * padding - kw_size) / stride + 1;                                     \
+        for (int f = 0; f < filters; ++f)                                                                      \
+            for (int c = 0; c < channels; ++c)                                                                 \
+                for (int kh = 0; kh < kh_size; ++kh)                                                           \
+                    for (int kw = 0; kw < kw_size; ++kw) {                                                     \
+                        ACC acc = 0;                                                                           \
+                        for (int n = 0; n < batch; ++n)                                                        \
+                            for (long oh = 0; oh < out_h; ++oh) {                                              \
+                                const long ih = oh * stride + kh - padding;                                    \
+                                if (ih < 0 || ih >= height) continue;                                          \
+                                for (long ow = 0; ow < out_w; ++ow) {                                          \
+                                    const long iw = ow * stride + kw - padding;                                \
+                                    if (iw < 0 || iw >= width) continue;                                       \
+                                    const float g = grad[(((size_t)n * filters + f) * out_h + oh) * out_w + ow]; \
+                                    const float x = input[(((size_t)n * channels + c) * height + ih) * width + iw]; \
+                                    acc = MAC(g, x, acc);                                                      \
+                                }                                                                              \
+                            }                                                                                  \
+                        weight_grad[(((size_t)f * channels + c) * kh_size + kh) * kw_size + kw] = acc;         \
+                    }                                                                                          \
+    }                                                                                                          \
+    ORACLE_API void oracle_conv2d_bias_backward_##NAME(int batch, int filters, int out_h, int out_w,          \
+                                                       const float* grad, ACC* bias_grad) {                    \
+        for (int f = 0; f < filters; ++f) {                                                                    \
+            ACC acc = 0;                                                                                       \
+            for (int n = 0; n < batch; ++n)                                                                    \
+                for (int oh = 0; oh < out_h; ++oh)                                                             \
+                    for (int ow = 0; ow < out_w; ++ow)                                                         \
+                        acc += grad[(((size_t)n * filters + f) * out_h + oh) * out_w + ow];                    \
+            bias_grad[f] = acc;                                                                                \
+        }                                                                                                      \
+    }
+
+#define ORACLE_FMA_F32(a, b, acc) fmaf((a), (b), (acc))
+#define ORACLE_MAC_F64(a, b, acc) ((acc) + (double)(a) * (double)(b))
+ORACLE_CONV_BWD(f32, float, ORACLE_FMA_F32)
+ORACLE_CONV_BWD(f64, double, ORACLE_MAC_F64)
+
+/*
  * Column-bias epilogue: a restatement of epilogue_col_bias_kernel
  * (src/ops/gemm/gemm_fused.cu:23-40): v = c + bias[col]; mode 1 ReLU, mode 2 tanh-GELU.
  */
