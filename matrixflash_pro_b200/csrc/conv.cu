@@ -316,24 +316,19 @@ __global__ void conv_bwd_filter_direct_kernel(const float* __restrict__ grad, co
     }
 }
 
-// dB[f] = sum over images and positions of dy[n][f]: one block per filter, per-thread partial
-// sums in a fixed stride pattern, then a fixed-order tree in shared memory (deterministic).
-__global__ void __launch_bounds__(256) conv_bwd_bias_kernel(const float* __restrict__ dy, int n, int kf,
-                                                            long long plane, float* __restrict__ db) {
-    __shared__ float part[256];
-    const int f = blockIdx.x;
+// dB[f] = sum over images, in image order, of the per-(image, filter) row sums.
+__global__ void conv_bias_images_kernel(const float* __restrict__ row_sums, int n, int kf, float* __restrict__ db) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= kf) return;
     float acc = 0.0f;
-    for (int img = 0; img < n; ++img) {
-        const float* src = dy + (static_cast<long long>(img) * kf + f) * plane;
-        for (long long j = threadIdx.x; j < plane; j += blockDim.x) acc += __ldg(src + j);
-    }
-    part[threadIdx.x] = acc;
-    __syncthreads();
-    for (int width = 128; width > 0; width >>= 1) {
-        if (threadIdx.x < width) part[threadIdx.x] += part[threadIdx.x + width];
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) db[f] = part[0];
+    for (int img = 0; img < n; ++img) acc += row_sums[static_cast<long long>(img) * kf + f];
+    db[f] = acc;
+}
+
+__global__ void conv_fill_kernel(float* __restrict__ p, long long count, float value) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        p[i] = value;
 }
 
 // ------------------------------------------------------------------------------------ tcgen05 conv table
@@ -602,9 +597,11 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     p.tiles_f = (k + e->bn - 1) / e->bn;
     p.ld_partial = p.tiles_f * e->bn;
     const long long total_kb = static_cast<long long>(n) * p.kb_per_img;
-    // About two work units per SM, each at least 16 K blocks long.
+    // Equal-length work units filling whole waves of the persistent grid: splits * tiles just
+    // under a multiple of the SM count (4 waves), each split at least 16 K blocks long.
     const int sms = sm_count(device);
-    long long splits = (2LL * sms + p.tiles_m * p.tiles_f - 1) / (p.tiles_m * p.tiles_f);
+    const long long out_tiles = static_cast<long long>(p.tiles_m) * p.tiles_f;
+    long long splits = std::max(1LL, (4LL * sms) / out_tiles);
     splits = std::max(1LL, std::min(splits, total_kb / 16));
     const long long kbs = (total_kb + splits - 1) / splits;
     splits = (total_kb + kbs - 1) / kbs;
@@ -683,10 +680,42 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     return MFB_OK;
 }
 
-mfb_status_t conv2d_bwd_bias_launch(cudaStream_t stream, int n, int k, int P, int Q, const float* dy, float* db) {
+// dB: the (N*K) x (P*Q) matrix dY times a ones vector on the GEMV path (row sums at the HBM
+// rate), then the images summed per filter in image order. Deterministic.
+mfb_status_t conv2d_bwd_bias_launch(int device, cudaStream_t stream, int n, int k, int P, int Q, const float* dy,
+                                    float* db) {
     if (k == 0) return MFB_OK;
-    conv_bwd_bias_kernel<<<k, 256, 0, stream>>>(dy, n, k, static_cast<long long>(P) * Q, db);
-    MFB_CUDA_TRY(cudaGetLastError(), "conv2d bias-gradient launch");
+    const long long plane = static_cast<long long>(P) * Q;
+    const long long rows = static_cast<long long>(n) * k;
+    if (rows == 0 || plane == 0) {
+        MFB_CUDA_TRY(cudaMemsetAsync(db, 0, static_cast<size_t>(k) * 4, stream), "dB clear");
+        return MFB_OK;
+    }
+    if (rows > 0x7fffffffLL || plane > 0x7fffffffLL) return fail(MFB_EUNSUPPORTED, "conv2d bias gradient too large");
+    mfb_gemm_desc d{};
+    d.m = static_cast<int>(rows);
+    d.n = 1;
+    d.k = static_cast<int>(plane);
+    d.lda = d.k;
+    d.ldb = 1;
+    d.ldc = 1;
+    d.alpha = 1.0f;
+    d.beta = 0.0f;
+    d.precision = MFB_PRECISION_FP32;
+    const size_t ones_bytes = static_cast<size_t>((plane + 63) / 64 * 64) * 4;
+    const size_t sums_bytes = static_cast<size_t>((rows + 63) / 64 * 64) * 4;
+    const size_t gemv_bytes = gemv_workspace_bytes(d);
+    void* ws = nullptr;
+    MFB_TRY(stream_workspace(device, stream, ones_bytes + sums_bytes + gemv_bytes, &ws));
+    float* ones = static_cast<float*>(ws);
+    float* sums = ones + ones_bytes / 4;
+    void* gemv_ws = gemv_bytes ? static_cast<void*>(sums + sums_bytes / 4) : nullptr;
+    conv_fill_kernel<<<static_cast<int>(std::min<long long>((plane + 255) / 256, 148LL * 4)), 256, 0, stream>>>(
+        ones, plane, 1.0f);
+    MFB_CUDA_TRY(cudaGetLastError(), "dB ones launch");
+    MFB_TRY(gemv_launch(d, stream, dy, ones, sums, nullptr, gemv_ws, gemv_bytes));
+    conv_bias_images_kernel<<<(k + 255) / 256, 256, 0, stream>>>(sums, n, k, db);
+    MFB_CUDA_TRY(cudaGetLastError(), "dB image-sum launch");
     return MFB_OK;
 }
 

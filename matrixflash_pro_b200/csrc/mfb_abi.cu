@@ -662,7 +662,7 @@ MFB_API mfb_status_t mfb_conv2d_bwd_bias(int device, mfb_stream_t stream_h, int 
     if (k > 0 && (!db || (n > 0 && p > 0 && q > 0 && !dy))) return fail(MFB_EINVAL, "null conv2d backward pointer");
     DeviceGuard guard;
     MFB_TRY(select_device(device));
-    return conv2d_bwd_bias_launch(reinterpret_cast<cudaStream_t>(stream_h), n, k, p, q, dy, db);
+    return conv2d_bwd_bias_launch(device, reinterpret_cast<cudaStream_t>(stream_h), n, k, p, q, dy, db);
 }
 
 }  // extern "C"

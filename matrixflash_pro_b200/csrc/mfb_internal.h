@@ -117,7 +117,8 @@ mfb_status_t conv2d_bwd_data_launch(int device, cudaStream_t stream, int n, int 
 mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r,
                                       int s, int stride, int pad, const float* x, const float* dy, float* dw,
                                       int precision);
-mfb_status_t conv2d_bwd_bias_launch(cudaStream_t stream, int n, int k, int P, int Q, const float* dy, float* db);
+mfb_status_t conv2d_bwd_bias_launch(int device, cudaStream_t stream, int n, int k, int P, int Q, const float* dy,
+                                    float* db);
 mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
                            int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
                            int precision);
