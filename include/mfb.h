@@ -17,6 +17,11 @@
  *   mfb_conv2d_bwd_data / _filter /  conv2d_input_backward / conv2d_weight_backward / conv2d_bias_backward
  *   mfb_conv2d_bwd_bias             include/matrix_pro/nn/conv.hpp:25-29 (kernels:
  *                                   src/nn/backward/convolution_kernels.cuh:9-95)
+ *   mfb_all_reduce / _broadcast /    matrix_pro::all_reduce / broadcast / all_gather / reduce_scatter /
+ *   _all_gather / _reduce_scatter /  scatter / gather (include/matrix_pro/distributed/collectives.hpp:20-32,
+ *   _scatter / _gather              src/hw/collectives.cpp:185-311)
+ *   mfb_cuda_nccl_allreduce         hw::cuda_nccl_allreduce (include/matrix_pro/detail/cuda_hooks.hpp:35,
+ *                                   stub at src/hw/cuda_backend.cu:252)
  *   mfb_covariance / mfb_correlation matrix_pro::covariance / correlation
  *                                   src/ops/reductions/covariance.inc:23-60
  *   mfb_plan_*                      GemmPlan ctor/execute/tune/rows/cols/inner/candidate_count
@@ -206,6 +211,34 @@ MFB_API mfb_status_t mfb_conv2d_bwd_filter(int device, mfb_stream_t stream, int 
                                            int precision);
 MFB_API mfb_status_t mfb_conv2d_bwd_bias(int device, mfb_stream_t stream, int n, int k, int p, int q, const float* dy,
                                          float* db);
+
+/* ---------------------------------------------------------------- collectives */
+/* One buffer per rank, all in this process (CollectiveBuffer of
+ * include/matrix_pro/distributed/collectives.hpp:22-26; device = CUDA device index). */
+typedef struct mfb_collective_buffer {
+    float* data;
+    size_t count;
+    int device;
+} mfb_collective_buffer;
+
+typedef enum mfb_reduce_op { MFB_REDUCE_SUM = 0, MFB_REDUCE_MEAN = 1, MFB_REDUCE_MAX = 2 } mfb_reduce_op;
+
+/* Blocking collectives with the reference's results in the reference's places (Mean = Sum x
+ * the float 1/rank_count; reduce_scatter leaves rank r's chunk in front of the all-reduced
+ * rest of its buffer; scatter/gather/all_gather move count_per_rank leading elements). Ranks
+ * on distinct GPUs run on one cached NCCL communicator per device set over NVLink/NVSwitch;
+ * ranks all on one GPU run device-local copies and a fixed-order reduction. Any other
+ * placement is MFB_EUNSUPPORTED. algorithm (0 ring, 1 tree) is accepted for compatibility;
+ * NCCL chooses its own. Work already queued on the devices finishes before the collective. */
+MFB_API mfb_status_t mfb_all_reduce(const mfb_collective_buffer* ranks, int rank_count, int op, int algorithm);
+MFB_API mfb_status_t mfb_broadcast(const mfb_collective_buffer* ranks, int rank_count, int root);
+MFB_API mfb_status_t mfb_all_gather(const mfb_collective_buffer* ranks, int rank_count, size_t count_per_rank);
+MFB_API mfb_status_t mfb_reduce_scatter(const mfb_collective_buffer* ranks, int rank_count, int op);
+MFB_API mfb_status_t mfb_scatter(const mfb_collective_buffer* ranks, int rank_count, int root, size_t count_per_rank);
+MFB_API mfb_status_t mfb_gather(const mfb_collective_buffer* ranks, int rank_count, int root, size_t count_per_rank);
+/* hw::cuda_nccl_allreduce: in-place all-reduce of ptrs[r] (count floats on devices[r]); op as above. */
+MFB_API mfb_status_t mfb_cuda_nccl_allreduce(float** ptrs, const int* devices, int rank_count, size_t count,
+                                             int reduce_op);
 
 /* ---------------------------------------------------------------- covariance / correlation */
 /* cov (cols x cols, row stride ldcov) = X_c^T X_c / max(rows - 1, 1), X_c = X minus its column

@@ -19,6 +19,7 @@ from .conv import (conv2d, conv2d_bias_backward, conv2d_input_backward, conv2d_i
 from .batch import (batch_matmul, batch_matmul_backward_left, batch_matmul_backward_right,  # noqa: F401
                     sgemm_strided_batched)
 from .stats import correlation, covariance  # noqa: F401
+from . import collectives  # noqa: F401
 from ._lib import LIB_PATH, lib  # noqa: F401
 
 __version__ = "0.1.0"

@@ -24,6 +24,8 @@ EXPORTED_SYMBOLS = (
     "mfb_plan_tune", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
     "mfb_conv2d_fwd", "mfb_naive_sgemm", "mfb_probe_wait_timeout", "mfb_covariance", "mfb_correlation",
     "mfb_probe_tf32_mma_tflops", "mfb_conv2d_bwd_data", "mfb_conv2d_bwd_filter", "mfb_conv2d_bwd_bias",
+    "mfb_all_reduce", "mfb_broadcast", "mfb_all_gather", "mfb_reduce_scatter", "mfb_scatter", "mfb_gather",
+    "mfb_cuda_nccl_allreduce",
 )
 
 
@@ -33,6 +35,11 @@ class GemmDesc(ctypes.Structure):
                 ("ldb", ctypes.c_int), ("ldc", ctypes.c_int), ("alpha", ctypes.c_float), ("beta", ctypes.c_float),
                 ("precision", ctypes.c_int), ("trans_a", ctypes.c_int), ("trans_b", ctypes.c_int),
                 ("epilogue", ctypes.c_int)]
+
+
+class CollectiveBuffer(ctypes.Structure):
+    """mfb_collective_buffer (include/mfb.h)."""
+    _fields_ = [("data", ctypes.c_void_p), ("count", ctypes.c_size_t), ("device", ctypes.c_int)]
 
 
 class PlanInfo(ctypes.Structure):
@@ -64,6 +71,14 @@ def _declare(lib):
         "mfb_cuda_device_count": (st, [ctypes.POINTER(ctypes.c_int)]),
         "mfb_sgemm": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_sgemm_noalloc": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
+        "mfb_all_reduce": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+        "mfb_broadcast": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int]),
+        "mfb_all_gather": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_size_t]),
+        "mfb_reduce_scatter": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int]),
+        "mfb_scatter": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int, ctypes.c_size_t]),
+        "mfb_gather": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int, ctypes.c_size_t]),
+        "mfb_cuda_nccl_allreduce": (st, [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                         ctypes.c_size_t, ctypes.c_int]),
         "mfb_conv2d_bwd_data": (st, [ctypes.c_int, _vp] + [ctypes.c_int] * 9 + [_vp, _vp, _vp, ctypes.c_int]),
         "mfb_conv2d_bwd_filter": (st, [ctypes.c_int, _vp] + [ctypes.c_int] * 9 + [_vp, _vp, _vp, ctypes.c_int]),
         "mfb_conv2d_bwd_bias": (st, [ctypes.c_int, _vp] + [ctypes.c_int] * 4 + [_vp, _vp]),

@@ -7,3 +7,4 @@
 #include "noalloc.cu"
 #include "stats.cu"
 #include "peak_probe.cu"
+#include "collectives.cu"

@@ -28,3 +28,10 @@ def test_host_tensors_are_rejected():
     """The product has no CPU path: host tensors fail loudly instead of computing."""
     with pytest.raises(mf.InvalidArgumentError):
         mf.sgemm_strided_batched(torch.ones(2, 3, 4), torch.ones(2, 4, 5), torch.empty(2, 3, 5))
+
+
+def test_collectives_reject_host_tensors():
+    with pytest.raises(mf.InvalidArgumentError):
+        mf.collectives.all_reduce([torch.ones(4), torch.ones(4)])
+    with pytest.raises(mf.InvalidArgumentError):
+        mf.collectives.broadcast([], 0)
