@@ -28,50 +28,69 @@ __device__ __forceinline__ float round_tf32(float x) {
 // hi + lo carries 22 significant bits of x. lo == nullptr writes only hi: the TF32
 // mode's operands, rounded to nearest like cuBLAS/CUTLASS TF32 conversion (the tensor
 // core itself would truncate the low 13 bits, a bias that shows on same-sign data).
-// blockIdx.y walks a strided batch: source matrix y at x + y * x_batch, its planes at
-// hi/lo + y * p_batch. shift (nullable, one value per stored column) is subtracted from
-// every element first: the column centering of covariance, fused into the split.
-__global__ void split_tf32_kernel(const float* __restrict__ x, long long ldx, int rows, int cols,
-                                  float* __restrict__ hi, float* __restrict__ lo, long long ldp, int vec_in,
-                                  long long x_batch, long long p_batch, const float* __restrict__ shift) {
-    x += blockIdx.y * x_batch;
-    hi += blockIdx.y * p_batch;
-    if (lo != nullptr) lo += blockIdx.y * p_batch;
-    const long long groups_per_row = ldp / 4;
-    const long long total = static_cast<long long>(rows) * groups_per_row;
-    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+// One operand's prepass: rows x cols of x (row stride ldx) into plane(s) of row stride ldp;
+// blockIdx.y walks a strided batch (source y at x + y * x_batch, planes at hi/lo + y * p_batch);
+// shift (nullable, one value per stored column) is subtracted first (covariance centering).
+struct SplitJob {
+    const float* x;
+    long long ldx;
+    int rows, cols;
+    float* hi;
+    float* lo;
+    long long ldp;
+    int vec_in;
+    long long x_batch, p_batch;
+    const float* shift;
+    int blocks;  // blocks of the launch's x dimension that serve this job
+};
+
+__device__ __forceinline__ void split_tf32_job(const SplitJob& j, int block, int nblocks) {
+    const float* x = j.x + blockIdx.y * j.x_batch;
+    float* hi = j.hi + blockIdx.y * j.p_batch;
+    float* lo = j.lo != nullptr ? j.lo + blockIdx.y * j.p_batch : nullptr;
+    const long long groups_per_row = j.ldp / 4;
+    const long long total = static_cast<long long>(j.rows) * groups_per_row;
+    for (long long idx = block * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(nblocks) * blockDim.x) {
         const long long r = idx / groups_per_row;
         const int c0 = static_cast<int>(idx - r * groups_per_row) * 4;
-        const float* src = x + r * ldx + c0;
+        const float* src = x + r * j.ldx + c0;
         float v[4];
-        if (vec_in && c0 + 3 < cols) {
+        if (j.vec_in && c0 + 3 < j.cols) {
             const float4 t = __ldg(reinterpret_cast<const float4*>(src));
             v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
         } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = (c0 + j < cols) ? __ldg(src + j) : 0.0f;
+            for (int e = 0; e < 4; ++e) v[e] = (c0 + e < j.cols) ? __ldg(src + e) : 0.0f;
         }
-        if (shift != nullptr) {
+        if (j.shift != nullptr) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = (c0 + j < cols) ? v[j] - __ldg(shift + c0 + j) : 0.0f;
+            for (int e = 0; e < 4; ++e) v[e] = (c0 + e < j.cols) ? v[e] - __ldg(j.shift + c0 + e) : 0.0f;
         }
         float4 h, l;
         if (lo != nullptr) {
             float hv[4], lv[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                hv[j] = round_tf32(v[j]);
-                lv[j] = round_tf32(v[j] - hv[j]);
+            for (int e = 0; e < 4; ++e) {
+                hv[e] = round_tf32(v[e]);
+                lv[e] = round_tf32(v[e] - hv[e]);
             }
             h = make_float4(hv[0], hv[1], hv[2], hv[3]);
             l = make_float4(lv[0], lv[1], lv[2], lv[3]);
-            *reinterpret_cast<float4*>(lo + r * ldp + c0) = l;
+            *reinterpret_cast<float4*>(lo + r * j.ldp + c0) = l;
         } else {
             h = make_float4(round_tf32(v[0]), round_tf32(v[1]), round_tf32(v[2]), round_tf32(v[3]));
         }
-        *reinterpret_cast<float4*>(hi + r * ldp + c0) = h;
+        *reinterpret_cast<float4*>(hi + r * j.ldp + c0) = h;
     }
+}
+
+// Both operands' prepasses in one launch: blocks [0, a.blocks) serve A, the rest B.
+__global__ void split_tf32_kernel(SplitJob a, SplitJob b) {
+    if (static_cast<int>(blockIdx.x) < a.blocks)
+        split_tf32_job(a, blockIdx.x, a.blocks);
+    else
+        split_tf32_job(b, blockIdx.x - a.blocks, b.blocks);
 }
 
 // C = beta * C (beta == 0 writes zeros without reading), then the column-bias epilogue.
@@ -349,6 +368,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     // [plane][batch entry][rows][cols rounded up to 4]. In the prepare-only phase a null
     // operand pointer skips that operand. ---
     PreparedOperand ops[2];
+    SplitJob jobs[2] = {};
     size_t used = 0;
     char* ws = static_cast<char*>(workspace);
     for (int which = 0; which < 2; ++which) {
@@ -370,17 +390,19 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         const int blocks = static_cast<int>(
             std::min<long long>((total_groups + 255) / 256, std::max(1LL, 148LL * 8 / nb)));
         const bool vec = ld % 4 == 0 && src_batch % 4 == 0 && aligned16(src);
-        if (run_prepass && blocks > 0 && src != nullptr) {
-            split_tf32_kernel<<<dim3(blocks, nb), 256, 0, stream>>>(src, ld, op.rows, op.cols, hi, lo, ldp,
-                                                                    vec ? 1 : 0, src_batch,
-                                                                    static_cast<long long>(pf), shift);
-            MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");
-        }
+        if (run_prepass && src != nullptr)
+            jobs[which] = SplitJob{src, ld, op.rows, op.cols, hi, lo, ldp, vec ? 1 : 0, src_batch,
+                                   static_cast<long long>(pf), shift, blocks};
         op.base = hi;
         op.ld = ldp;
         op.plane_stride = cfg.planes == 2 ? static_cast<long long>(pf) * nb : 0;
         op.batch_stride = static_cast<long long>(pf);
         op.needs_prepass = true;
+    }
+    if (jobs[0].blocks + jobs[1].blocks > 0) {
+        if (jobs[0].blocks == 0) std::swap(jobs[0], jobs[1]);  // a lone B job runs as the first
+        split_tf32_kernel<<<dim3(jobs[0].blocks + jobs[1].blocks, nb), 256, 0, stream>>>(jobs[0], jobs[1]);
+        MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");
     }
     if (!run_gemm) return MFB_OK;
 

@@ -149,6 +149,8 @@ class RowSplitGemm:
         sched = PanelSchedule(self.sched.panels, [beta] + [1.0] * (len(self.sched.panels) - 1), self.sched.sm_limits)
         self.kernel_events = []
 
+        split_a_early = self.world > 1
+
         def prepare_a(i, panel):
             # A's split/rounding prepass does not read B: it runs while B is in flight.
             self.plans[i].prepare(stream, a0 + 4 * panel[0], 0)
@@ -158,7 +160,8 @@ class RowSplitGemm:
             plan = self.plans[i]
             a_ptr = a0 + 4 * k0
             b_ptr = b0 + 4 * k0 * self.ldb
-            plan.prepare(stream, 0, b_ptr)
+            # one prepass launch for both operands unless A's was issued during the broadcast
+            plan.prepare(stream, 0 if split_a_early else a_ptr, b_ptr)
             plan.set_sm_limit(sm_limit)
             if time_kernels:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -171,12 +174,13 @@ class RowSplitGemm:
         def b_rows(k0, k1):
             return B.as_strided((k1 - k0, self.ldb), (self.ldb, 1), B.storage_offset() + k0 * self.ldb)
 
-        run_schedule(sched, b_rows, panel_gemm, self.group, self.src, before_wait=prepare_a)
+        run_schedule(sched, b_rows, panel_gemm, self.group, self.src,
+                     before_wait=prepare_a if split_a_early else None)
 
     def launches_per_step(self) -> int:
-        """Kernels of this library per step: the prepass of A (hi/lo split, or TF32 rounding),
-        the prepass of B and the GEMM, per panel."""
-        return 3 * len(self.plans)
+        """Kernels of this library per step, per panel: the operand prepass (hi/lo split, or TF32
+        rounding; A's separately while B is broadcast) and the GEMM."""
+        return (3 if self.world > 1 else 2) * len(self.plans)
 
     def kernel_ms(self) -> float:
         return sum(e0.elapsed_time(e1) for (e0, e1) in self.kernel_events)
