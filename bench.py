@@ -48,6 +48,30 @@ WORKLOADS = {
 }
 
 
+def link_roofline(torch, h2d_bytes, d2h_bytes, ms_per_step, nbytes=256 << 20, reps=3):
+    """PCIe bound of an end-to-end step: pinned host<->device copy rates measured here (each
+    direction alone, CUDA events), and the step time those rates allow for the step's bytes."""
+    h = torch.empty(nbytes // 4, dtype=torch.float32, pin_memory=True)
+    d = torch.empty(nbytes // 4, dtype=torch.float32, device="cuda")
+    rates = {}
+    for name, fn in (("h2d_gbs", lambda: d.copy_(h, non_blocking=True)),
+                     ("d2h_gbs", lambda: h.copy_(d, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        rates[name] = nbytes * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
+    bound = max(h2d_bytes / rates["h2d_gbs"], d2h_bytes / rates["d2h_gbs"]) / 1e6
+    return {"h2d_gbs": rates["h2d_gbs"], "d2h_gbs": rates["d2h_gbs"], "bound_ms": bound,
+            "ms_per_step": ms_per_step, "frac": bound / ms_per_step if ms_per_step > 0 else None,
+            "basis": "max(h2d bytes / h2d rate, d2h bytes / d2h rate), rates of 256 MiB pinned copies "
+                     "each direction alone"}
+
+
 def read_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -515,7 +539,8 @@ def run_aux_workload(args):
         s1.record()
         torch.cuda.synchronize()
         e2e = {"value": work * args.e2e_steps / (s0.elapsed_time(s1) / 1e3) / metric_unit, "unit": unit,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps}
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps,
+               "link": link_roofline(torch, h2d, d2h, s0.elapsed_time(s1) / args.e2e_steps)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -634,17 +659,22 @@ def main():
         A_h.copy_(A_buf)
         B_h.copy_(B_buf)
         C_h.copy_(C_buf)
-        C_out = torch.empty_like(C_h).pin_memory()
-        h2d = A_h.numel() * 4 + C_h.numel() * 4 + (B_h.numel() * 4 if rank == 0 else 0)
-        d2h = C_out.numel() * 4
+        A_hv, B_hv, C_hv = A_h[:, :k], B_h[:, :n], C_h[:, :n]
+        opts = mf.GemmOptions(precision=precision)
+        # mfb_sgemm_host streams rows of A and C through the GPU in panels (copies overlap the
+        # GEMM) and returns C into the same pinned host matrix. B: from host on one GPU; with
+        # several, rank 0 copies it in and broadcasts it over NVLink, as RowSplitGemm takes it.
+        h2d = 4 * (m * k + (m * n if beta != 0.0 else 0) + (k * n if rank == 0 else 0))
+        d2h = 4 * m * n
 
         def e2e_step():
-            A_buf.copy_(A_h, non_blocking=True)
+            if world == 1:
+                mf.sgemm_host(A_hv, B_hv, C_hv, alpha, beta, opts)
+                return
             if rank == 0:
                 B_buf.copy_(B_h, non_blocking=True)
-            C_buf.copy_(C_h, non_blocking=True)
-            op(A, B, C, alpha, beta)
-            C_out.copy_(C_buf, non_blocking=True)
+            dist.broadcast(B_buf, src=0)
+            mf.sgemm_host(A_hv, B, C_hv, alpha, beta, opts)
 
         e2e_step()
         torch.cuda.synchronize()
@@ -663,7 +693,10 @@ def main():
         e2e_ms = float(t2.item())
         e2e = {"value": world * flops_per_rank_step * args.e2e_steps / (e2e_ms / 1e3) / 1e12, "unit": "TFLOPS",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps,
-               "path": "pinned host A/B/C -> device, RowSplitGemm (C ABI plans), device C -> pinned host"}
+               "path": "mfb_sgemm_host on pinned host A/B/C (row panels of A and C copied in and C copied out "
+                       "on copy streams while the GEMM of the previous panel runs)"
+                       + ("" if world == 1 else "; B copied in on rank 0 and broadcast (NCCL)"),
+               "link": link_roofline(torch, h2d, d2h, e2e_ms / args.e2e_steps)}
 
     # ---------------------------------------------------------------- roofline of the GEMM kernel
     peaks, peak_src = read_peaks()

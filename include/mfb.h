@@ -12,6 +12,8 @@
  *                                   (body: src/hw/cuda_backend.cu:91-99,159-163)
  *   mfb_sgemm                       the cublasLtMatmul/cublasGemmEx call of GemmPlan::Impl::run_ptr
  *                                   src/ops/gemm/plan/implementation.inc:128-151
+ *   mfb_sgemm_host                  the GPU share of HeterogeneousScheduler::gemm (host operands)
+ *                                   src/hw/scheduler.cpp:236-312
  *   mfb_sgemm_strided_batched       cublasSgemmStridedBatched in batch_matmul and its backward
  *                                   src/nn/batch.cu:12-35, src/nn/backward/batched_matmul.inc:7-55
  *   mfb_conv2d_bwd_data / _filter /  conv2d_input_backward / conv2d_weight_backward / conv2d_bias_backward
@@ -125,6 +127,19 @@ MFB_API mfb_status_t mfb_cuda_device_count(int* count);
  * (CUDA graph capture) create a plan. bias: n floats, required iff epilogue != NONE. */
 MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
                                const float* b, float* c, const float* bias);
+
+/* ---------------------------------------------------------------- GEMM on host operands */
+/* mfb_sgemm where each of A, B, C and bias may be host memory (pinned for full PCIe speed;
+ * pageable works, staged by the driver) or memory of `device`: the GPU share of the
+ * reference's host-side GEMM, HeterogeneousScheduler::gemm (src/hw/scheduler.cpp:236-312),
+ * which copies B, A and C in, runs hw::cuda_gemm and copies C out one step after another.
+ * Here B and the bias are copied once, and the rows of C stream through a ring of device
+ * panels: copy-in of panel i, the GEMM of panel i-1 and copy-out of panel i-2 run at once
+ * (two library-owned copy streams, the GEMM on `stream`). Stream-ordered: host C holds the
+ * result once `stream` is synchronized. Device buffers are cached per device and grow on
+ * demand; calls on one device are serialized. */
+MFB_API mfb_status_t mfb_sgemm_host(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
+                                    const float* b, float* c, const float* bias);
 
 /* ---------------------------------------------------------------- strided-batched GEMM */
 /* batch_count GEMMs that share one descriptor: C_i = epilogue(alpha op(A_i) op(B_i) + beta C_i)

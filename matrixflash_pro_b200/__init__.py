@@ -12,7 +12,7 @@ from .errors import (CudaError, DeviceTimeoutError, InvalidArgumentError, Matrix
 from .gemm import (GemmEpilogue, GemmOptions, GemmPlan, GemmPrecision, GemmTuningResult, checked_dim, cuda_gemm,  # noqa: F401,E501
                    cuda_sync, device_status, gemm, gemm_bias_gelu, gemm_bias_relu, gemm_into, gemv,
                    get_wait_limit_ns, make_desc, multiply, multiply_into, naive_sgemm, probe_tf32_mma_tflops,
-                   set_wait_limit_ns, sgemm,
+                   set_wait_limit_ns, sgemm, sgemm_host,
                    sgemm_ptr, sync)
 from .conv import (conv2d, conv2d_bias_backward, conv2d_input_backward, conv2d_into, conv2d_out_shape,  # noqa: F401
                    conv2d_weight_backward)

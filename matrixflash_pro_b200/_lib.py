@@ -18,7 +18,7 @@ MFB_OK, MFB_EINVAL, MFB_ECUDA, MFB_ETIMEOUT, MFB_ENCCL, MFB_EUNSUPPORTED, MFB_EN
 # Every symbol include/mfb.h declares, in header order.
 EXPORTED_SYMBOLS = (
     "mfb_status_string", "mfb_last_error", "mfb_version", "mfb_device_status", "mfb_set_wait_limit_ns",
-    "mfb_get_wait_limit_ns", "mfb_sync", "mfb_cuda_gemm", "mfb_cuda_sync", "mfb_cuda_device_count", "mfb_sgemm",
+    "mfb_get_wait_limit_ns", "mfb_sync", "mfb_cuda_gemm", "mfb_cuda_sync", "mfb_cuda_device_count", "mfb_sgemm", "mfb_sgemm_host",
     "mfb_sgemm_noalloc", "mfb_sgemm_strided_batched",
     "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_set_sm_limit",
     "mfb_plan_tune", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
@@ -70,6 +70,7 @@ def _declare(lib):
         "mfb_cuda_sync": (st, [ctypes.c_int]),
         "mfb_cuda_device_count": (st, [ctypes.POINTER(ctypes.c_int)]),
         "mfb_sgemm": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
+        "mfb_sgemm_host": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_sgemm_noalloc": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_all_reduce": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "mfb_broadcast": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int]),

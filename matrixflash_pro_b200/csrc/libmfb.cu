@@ -8,3 +8,4 @@
 #include "stats.cu"
 #include "peak_probe.cu"
 #include "collectives.cu"
+#include "host_gemm.cu"

@@ -74,11 +74,12 @@ def _stream_handle(stream=None) -> int:
     return int(s.cuda_stream)
 
 
-def _ld(t: torch.Tensor, what: str) -> int:
-    """Leading dimension of a row-major (possibly row-padded) 2-D float32 CUDA tensor."""
+def _ld(t: torch.Tensor, what: str, host_ok: bool = False) -> int:
+    """Leading dimension of a row-major (possibly row-padded) 2-D float32 CUDA tensor (or CPU
+    tensor, where the entry point accepts host memory)."""
     if t.dtype != torch.float32:
         raise InvalidArgumentError(f"{what} must be float32")
-    if not t.is_cuda:
+    if not t.is_cuda and not host_ok:
         raise InvalidArgumentError(f"{what} must be a CUDA tensor")
     if t.dim() != 2:
         raise ShapeMismatchError(f"{what} must be a matrix")
@@ -172,6 +173,43 @@ def sgemm(left: torch.Tensor, right: torch.Tensor, out: torch.Tensor, alpha: flo
                      int(o.transpose_right), int(o.epilogue))
     _check_bias(o, bias, n)
     sgemm_ptr(out.device.index, _stream_handle(stream), desc, _ptr(left), _ptr(right), _ptr(out), _ptr(bias))
+    return out
+
+
+def sgemm_host(left: torch.Tensor, right: torch.Tensor, out: torch.Tensor, alpha: float = 1.0, beta: float = 0.0,
+               options: GemmOptions | None = None, bias: torch.Tensor | None = None, device: int | None = None,
+               stream=None) -> torch.Tensor:
+    """out = epilogue(alpha*op(left)*op(right) + beta*out) where each operand may be a CPU tensor
+    (pinned memory copies at full PCIe speed) or a tensor on `device`: the GPU share of the
+    reference's host-side GEMM (HeterogeneousScheduler::gemm, src/hw/scheduler.cpp:236-312),
+    with the rows of out streamed through the GPU in panels so the copies overlap the GEMM
+    (mfb_sgemm_host). Stream-ordered: a CPU `out` holds the result once `stream` (default: the
+    current stream) has been synchronized."""
+    o = options or GemmOptions()
+    m, n, k, k2 = _gemm_dims(left, right, o)
+    if k != k2:
+        raise ShapeMismatchError("GEMM inner dimension mismatch")
+    if tuple(out.shape) != (m, n):
+        raise ShapeMismatchError("GEMM output shape mismatch")
+    for t, what in ((left, "left"), (right, "right"), (out, "output")):
+        if t.dtype != torch.float32:
+            raise InvalidArgumentError(f"{what} must be float32")
+    if o.epilogue != GemmEpilogue.none:
+        if bias is None or bias.numel() != n:
+            raise ShapeMismatchError("GEMM bias length must equal N")
+        if bias.dtype != torch.float32 or not bias.is_contiguous():
+            raise InvalidArgumentError("GEMM bias must be a contiguous float32 tensor")
+    cuda = [t.device.index for t in (left, right, out, bias) if t is not None and t.is_cuda]
+    dev = cuda[0] if cuda else (torch.cuda.current_device() if device is None else device)
+    if any(i != dev for i in cuda):
+        raise InvalidArgumentError("device operands of sgemm_host must share one device")
+    desc = make_desc(checked_dim(m), checked_dim(n), checked_dim(k), _ld(left, "left", True),
+                     _ld(right, "right", True), _ld(out, "output", True), alpha, beta, int(o.precision),
+                     int(o.transpose_left), int(o.transpose_right), int(o.epilogue))
+    with torch.cuda.device(dev):
+        handle = _stream_handle(stream)
+    _lib.check(_lib.lib().mfb_sgemm_host(dev, handle, ctypes.byref(desc), _ptr(left), _ptr(right), _ptr(out),
+                                         _ptr(bias)), "sgemm_host")
     return out
 
 

@@ -62,9 +62,10 @@ def _desc(**kw):
 def test_sgemm_rejects_bad_descriptors(kw, expected, needle):
     lib = mf.lib()
     d = _desc(**kw)
-    st = lib.mfb_sgemm(0, None, ctypes.byref(d), 16, 32, 48, 0)
-    assert st == expected
-    assert needle in _lib.last_error()
+    for entry in (lib.mfb_sgemm, lib.mfb_sgemm_host):  # checked before any CUDA call
+        st = entry(0, None, ctypes.byref(d), 16, 32, 48, 0)
+        assert st == expected
+        assert needle in _lib.last_error()
 
 
 def test_sgemm_rejects_alias_and_missing_bias():
