@@ -87,6 +87,7 @@ __device__ __forceinline__ void split_tf32_job(const SplitJob& j, int block, int
 
 // Both operands' prepasses in one launch: blocks [0, a.blocks) serve A, the rest B.
 __global__ void split_tf32_kernel(SplitJob a, SplitJob b) {
+    grid_launch_dependents();  // the GEMM that follows may set up while this grid drains
     if (static_cast<int>(blockIdx.x) < a.blocks)
         split_tf32_job(a, blockIdx.x, a.blocks);
     else
@@ -399,7 +400,8 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         op.batch_stride = static_cast<long long>(pf);
         op.needs_prepass = true;
     }
-    if (jobs[0].blocks + jobs[1].blocks > 0) {
+    const bool prepass_launched = jobs[0].blocks + jobs[1].blocks > 0;
+    if (prepass_launched) {
         if (jobs[0].blocks == 0) std::swap(jobs[0], jobs[1]);  // a lone B job runs as the first
         split_tf32_kernel<<<dim3(jobs[0].blocks + jobs[1].blocks, nb), 256, 0, stream>>>(jobs[0], jobs[1]);
         MFB_CUDA_TRY(cudaGetLastError(), "split/pack prepass launch");
@@ -454,20 +456,31 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
                          "cudaFuncSetAttribute(cluster size)");
     }
     void* args[] = {&map_a, &map_b, &p};
+    // Right after this call's prepass the GEMM launches programmatically: its CTAs set up
+    // (barriers, TMEM, descriptor prefetch) while the prepass drains, then wait for it.
+    cudaLaunchAttribute pdl;
+    pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl.val.programmaticStreamSerializationAllowed = 1;
     if (!e->pair) {
         const long long grid = std::min<long long>(tiles, sms);
-        MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(static_cast<unsigned>(grid)), dim3(e->threads), args,
-                                      static_cast<size_t>(e->smem), stream),
-                     "tcgen05 GEMM launch");
+        cudaLaunchConfig_t lc{};
+        lc.gridDim = dim3(static_cast<unsigned>(grid));
+        lc.blockDim = dim3(e->threads);
+        lc.dynamicSmemBytes = static_cast<size_t>(e->smem);
+        lc.stream = stream;
+        lc.attrs = &pdl;
+        lc.numAttrs = prepass_launched ? 1 : 0;
+        MFB_CUDA_TRY(cudaLaunchKernelExC(&lc, e->fn, args), "tcgen05 GEMM launch");
         return MFB_OK;
     }
     // SM pairs: clusters of 2 CTAs, as many as can be co-resident (capped by the SM limit).
     cudaLaunchConfig_t lc{};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1] = pdl;
     lc.blockDim = dim3(e->threads);
     lc.dynamicSmemBytes = static_cast<size_t>(e->smem);
     lc.stream = stream;
@@ -492,6 +505,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     const long long pairs = std::min<long long>({tiles, static_cast<long long>(max_clusters),
                                                  static_cast<long long>(std::max(1, sms / 2))});
     lc.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    lc.numAttrs = prepass_launched ? 2 : 1;
     MFB_CUDA_TRY(cudaLaunchKernelExC(&lc, e->fn, args), "tcgen05 pair GEMM launch");
     return MFB_OK;
 }

@@ -95,6 +95,12 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
     return mbar_wait_bounded(bar, parity, limit_ns, nullptr);
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while the previous kernel of the stream still runs; it waits here, before its
+// first access to memory that kernel writes. Without the launch attribute both are no-ops.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void report_status(uint32_t bits, volatile int* abort) {
     atomicOr(&g_status, bits);
     if (abort) *abort = 1;

@@ -227,6 +227,7 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint64_t limit = p.wait_limit_ns;
+    grid_dependency_wait();  // operands written by the preceding prepass (programmatic launch)
 
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------------ TMA producer

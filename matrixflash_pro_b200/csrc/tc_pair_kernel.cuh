@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint64_t limit = p.wait_limit_ns;
+    grid_dependency_wait();  // operands written by the preceding prepass (programmatic launch)
 
     auto give_up = [&](uint32_t bits) {
         report_status(bits, abort_flag);
