@@ -41,69 +41,90 @@ __device__ __forceinline__ void write_planes4(float* hi, float* lo, long long of
 
 // x (N,C,H,W) -> X [N][Hp*Wp][Cp]: zero border of `pad`, zero channels in [C, Cp).
 // grid (ceil(Hp / kPackRows), ceil(Cp / 32), N): a block takes kPackRows padded rows of
-// 32 channels. Input rows are read whole (128-bit loads when W and the row base allow),
-// transposed in shared memory (odd row stride: conflict-free column reads) and written
-// as 128-byte channel rows of every padded position, border zeros included.
+// 32 channels. Phase 1: each warp reads whole input rows of one channel (64-bit loads when
+// W is even and the image is 8-byte aligned) and stores them transposed, [row][iw][33];
+// the odd position stride keeps the channel reads of phase 2 conflict-free. Phase 2 writes
+// one float4 of 4 channels per (padded position, group) as 128-byte channel rows; border
+// positions and channels >= C become zeros there, so the tile is never zero-filled. The
+// kernel is issue-bound unless its index arithmetic stays out of the inner loops: no
+// division, 32-bit offsets from a per-block base, guards hoisted.
 constexpr int kPackRows = 2;
+constexpr int kPackStride = 33;
 constexpr int kPackMaxWp = 512;  // padded width the shared tile holds; wider images use the generic kernel
 
+size_t pack_rows_smem_bytes(int w) { return static_cast<size_t>(kPackRows) * w * kPackStride * 4; }
+
 __global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __restrict__ x, int c, int h, int w,
-                                                             int pad_h, int pad_w, int cp, int hp, int wp, int vec,
+                                                             int pad_h, int pad_w, int cp, int hp, int wp, int vec2,
                                                              float* __restrict__ hi, float* __restrict__ lo) {
-    extern __shared__ float tile[];  // [32][stride], stride = kPackRows * wp rounded up to odd
-    const int stride = (kPackRows * wp) | 1;
+    extern __shared__ float tile[];  // [kPackRows][w][kPackStride]
     const int pr0 = blockIdx.x * kPackRows;
     const int c0 = blockIdx.y * 32;
     const int img = blockIdx.z;
     const int rows = min(kPackRows, hp - pr0);
-    // Phase 1: input rows -> tile (zeros for border columns, border rows and channels >= C).
-    const int w4 = vec ? w / 4 : 0;
-    for (int i = threadIdx.x; i < 32 * rows * wp; i += blockDim.x) {
-        const int cc = i / (rows * wp);
-        const int rem = i - cc * rows * wp;
-        tile[cc * stride + rem] = 0.0f;
-    }
-    __syncthreads();
-    if (vec) {
-        for (int i = threadIdx.x; i < 32 * rows * w4; i += blockDim.x) {
-            const int cc = i / (rows * w4);
-            const int rem = i - cc * rows * w4;
-            const int rr = rem / w4;
-            const int q4 = rem - rr * w4;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Phase 1: input rows -> transposed tile (rows outside the image and channels >= C are skipped).
+    // Warp w owns the channel rows (task) w, w + 8, ..., w + 56 (task = rr * 32 + channel); all
+    // eight loads of a lane are issued before any shared-memory store, so each SM keeps
+    // ~128 KB of loads in flight.
+    const int ntask = 32 * rows;
+    const int units = vec2 ? w / 2 : w;  // float2 or float units per channel row
+    for (int jc = 0; jc < units; jc += 32) {
+        const int j = jc + lane;
+        float2 v[8];
+        bool ok[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int task = warp + 8 * u;
+            const int cc = task & 31, rr = task >> 5;
             const int ih = pr0 + rr - pad_h, ch = c0 + cc;
-            if (ih >= 0 && ih < h && ch < c) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(
-                    x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + 4 * q4));
-                float* dst = tile + cc * stride + rr * wp + pad_w + 4 * q4;
-                dst[0] = v.x;
-                dst[1] = v.y;
-                dst[2] = v.z;
-                dst[3] = v.w;
+            ok[u] = task < ntask && j < units && ih >= 0 && ih < h && ch < c;
+            v[u] = make_float2(0.0f, 0.0f);
+            if (ok[u]) {
+                const float* src = x + ((static_cast<long long>(img) * c + ch) * h + ih) * w;
+                if (vec2) v[u] = __ldg(reinterpret_cast<const float2*>(src) + j);
+                else v[u].x = __ldg(src + j);
             }
         }
-    } else {
-        for (int i = threadIdx.x; i < 32 * rows * w; i += blockDim.x) {
-            const int cc = i / (rows * w);
-            const int rem = i - cc * rows * w;
-            const int rr = rem / w;
-            const int iw = rem - rr * w;
-            const int ih = pr0 + rr - pad_h, ch = c0 + cc;
-            if (ih >= 0 && ih < h && ch < c)
-                tile[cc * stride + rr * wp + pad_w + iw] =
-                    __ldg(x + ((static_cast<long long>(img) * c + ch) * h + ih) * w + iw);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (!ok[u]) continue;
+            const int task = warp + 8 * u;
+            const int cc = task & 31, rr = task >> 5;
+            if (vec2) {
+                float* dst = tile + (rr * w + 2 * j) * kPackStride + cc;
+                dst[0] = v[u].x;
+                dst[kPackStride] = v[u].y;
+            } else {
+                tile[(rr * w + j) * kPackStride + cc] = v[u].x;
+            }
         }
     }
     __syncthreads();
-    // Phase 2: one float4 of 4 channels per (position, group); 8 groups cover 32 channels.
-    const long long npos = static_cast<long long>(hp) * wp;
-    const int groups = min(8, (cp - c0) / 4);
-    for (int i = threadIdx.x; i < rows * wp * 8; i += blockDim.x) {
-        const int pos = i / 8, q = i % 8;
-        if (q >= groups) continue;
-        const long long off = (static_cast<long long>(img) * npos + static_cast<long long>(pr0) * wp + pos) * cp +
-                              c0 + 4 * q;
-        const float* t = tile + 4 * q * stride + pos;
-        write_planes4(hi, lo, off, t[0], t[stride], t[2 * stride], t[3 * stride]);
+    // Phase 2: thread t writes channel group q = t % 8 (4 channels) of positions t / 8, +32, ...
+    // Offsets are 32-bit from a per-block base; every guard is hoisted out of the loop.
+    const int q = threadIdx.x & 7;
+    if (q >= min(8, (cp - c0) / 4)) return;
+    const long long base = (static_cast<long long>(img) * hp + pr0) * wp * cp + c0 + 4 * q;
+    const int nch = min(4, c - (c0 + 4 * q));  // real channels of this group (<= 0: all zero)
+    for (int rr = 0; rr < rows; ++rr) {
+        const int ih = pr0 + rr - pad_h;
+        const bool row_in = ih >= 0 && ih < h && nch > 0;
+        const float* trow = tile + rr * w * kPackStride + 4 * q;
+        float* hrow = hi + base + static_cast<long long>(rr) * wp * cp;
+        float* lrow = lo ? lo + base + static_cast<long long>(rr) * wp * cp : nullptr;
+        for (int pw = threadIdx.x >> 3; pw < wp; pw += 32) {
+            const int iw = pw - pad_w;
+            float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f, v3 = 0.0f;
+            if (row_in && static_cast<unsigned>(iw) < static_cast<unsigned>(w)) {
+                const float* t = trow + iw * kPackStride;
+                v0 = t[0];
+                v1 = nch > 1 ? t[1] : 0.0f;
+                v2 = nch > 2 ? t[2] : 0.0f;
+                v3 = nch > 3 ? t[3] : 0.0f;
+            }
+            write_planes4(hrow, lrow, static_cast<long long>(pw) * cp, v0, v1, v2, v3);
+        }
     }
 }
 
@@ -441,13 +462,13 @@ mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g,
     float* b_hi = a_hi + planes * a_plane;
     float* b_lo = planes == 2 ? b_hi + b_plane : nullptr;
     if (wp <= kPackMaxWp) {
-        const size_t tile_bytes = static_cast<size_t>(32) * ((kPackRows * wp) | 1) * 4;
+        const size_t tile_bytes = pack_rows_smem_bytes(w);
         if (tile_bytes > 48 * 1024)
             MFB_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(&conv_pack_rows_kernel),
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               static_cast<int>(tile_bytes)),
                          "conv prepass smem attribute");
-        const int vec = (w % 4 == 0 && aligned16(x)) ? 1 : 0;
+        const int vec = (w % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) ? 1 : 0;
         dim3 pgrid(static_cast<unsigned>((hp + kPackRows - 1) / kPackRows), static_cast<unsigned>((cp + 31) / 32), n);
         conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, g.pad_h, g.pad_w, cp, hp, wp, vec,
                                                                  a_hi, a_lo);
@@ -624,13 +645,13 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
 
     // X planes (as the forward), dY planes in X's padded width.
     if (wp <= kPackMaxWp) {
-        const size_t tile_bytes = static_cast<size_t>(32) * ((kPackRows * wp) | 1) * 4;
+        const size_t tile_bytes = pack_rows_smem_bytes(w);
         if (tile_bytes > 48 * 1024)
             MFB_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(&conv_pack_rows_kernel),
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               static_cast<int>(tile_bytes)),
                          "conv prepass smem attribute");
-        const int vec = (w % 4 == 0 && aligned16(x)) ? 1 : 0;
+        const int vec = (w % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) ? 1 : 0;
         dim3 pgrid(static_cast<unsigned>((hp + kPackRows - 1) / kPackRows), static_cast<unsigned>((cp + 31) / 32), n);
         conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, pad, pad, cp, hp, wp, vec, a_hi, a_lo);
     } else {
