@@ -7,7 +7,7 @@ B ~ N(0, 1/64) (std 1/sqrt(4096)), C ~ N(0,1), alpha=0.5, beta=1, strict FP32
 (3xTF32 on tcgen05). One step = one pass of the hot path over one batch:
 split prepass + tcgen05 GEMM; with N > 1 GPUs each rank owns 8192 rows of A and C
 (weak scaling) and B is broadcast from rank 0 over NVLink by NCCL inside the step,
-in K panels overlapped with the per-panel GEMM.
+in column panels overlapped with the per-panel GEMM.
 
 Prints ONE JSON line (rank 0). `--impl reference` times the reference's own CPU
 gemm_f32 (oracle/_ref, built from the reference sources) on the same configuration.
@@ -729,7 +729,7 @@ def main():
     peak_used = peak_sust if long_run else peak_burst
     gemm_flops = flops_per_rank_step * args.steps
     achieved = gemm_flops / (kernel_ms / 1e3) / 1e12 if kernel_ms > 0 else None
-    launches_gemm = len(op.plans) * args.steps
+    launches_gemm = op.gemm_launches_per_step() * args.steps
     tag = f"gemm_{'3xtf32' if strict else 'tf32'}_{args.workload}"
     traffic = read_profile_traffic(tag)
     basis = "bf16_tflops_sustained" if long_run else "bf16_tflops"
@@ -767,7 +767,7 @@ def main():
             "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": desc, "m_per_gpu": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "ldc": ldc,
                        "precision": "strict fp32 (3xTF32 tcgen05)" if strict else "tf32 (tcgen05)",
-                       "parallelism": f"row-split x{world}" + (", B broadcast by NCCL in K panels" if world > 1
+                       "parallelism": f"row-split x{world}" + (", B broadcast by NCCL in column panels" if world > 1
                                                                else ""),
                        "l2": (f"step footprint {footprint / 2**20:.0f} MiB < 2 x L2: L2 flushed by a "
                               f"{FLUSH_BYTES >> 20} MiB write between steps, each step timed alone by CUDA "

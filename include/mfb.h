@@ -199,8 +199,18 @@ MFB_API mfb_status_t mfb_plan_execute(mfb_plan_t plan, mfb_stream_t stream, cons
 MFB_API mfb_status_t mfb_plan_prepare(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b);
 MFB_API mfb_status_t mfb_plan_multiply(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
                                        float* c, float alpha, float beta, const float* bias);
+/* Column-range phases, for a caller that receives B in column blocks (the row-split GEMM
+ * broadcasts B in contiguous column panels): prepare_cols splits B's columns [n0, n1),
+ * given as their own k x (n1 - n0) matrix with row stride ldb, into the plan's B planes;
+ * multiply_cols computes only C's columns [n0, n1) (A prepared by mfb_plan_prepare, the
+ * columns' B by prepare_cols). tcgen05 plans with a non-transposed B; n0 and n1 (unless
+ * n1 == n) multiples of 32. No reference counterpart. */
+MFB_API mfb_status_t mfb_plan_prepare_cols(mfb_plan_t plan, mfb_stream_t stream, const float* b, int ldb,
+                                           int n0, int n1);
+MFB_API mfb_status_t mfb_plan_multiply_cols(mfb_plan_t plan, mfb_stream_t stream, const float* a, float* c,
+                                            float alpha, float beta, const float* bias, int n0, int n1);
 /* Caps the persistent GEMM grid at `sms` SMs (0 = all), leaving the rest to work that
- * must run concurrently, e.g. an NCCL broadcast of the next K panel. */
+ * must run concurrently, e.g. an NCCL broadcast of the next column panel of B. */
 MFB_API mfb_status_t mfb_plan_set_sm_limit(mfb_plan_t plan, int sms);
 /* Times every admissible tile configuration on `scratch_c` (an m x n buffer with ldc
  * of the plan; c is never touched), keeps the fastest, and reports it. Synchronizes. */

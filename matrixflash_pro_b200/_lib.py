@@ -20,7 +20,8 @@ EXPORTED_SYMBOLS = (
     "mfb_status_string", "mfb_last_error", "mfb_version", "mfb_device_status", "mfb_set_wait_limit_ns",
     "mfb_get_wait_limit_ns", "mfb_sync", "mfb_cuda_gemm", "mfb_cuda_sync", "mfb_cuda_device_count", "mfb_sgemm", "mfb_sgemm_host",
     "mfb_sgemm_noalloc", "mfb_sgemm_strided_batched",
-    "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_set_sm_limit",
+    "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_prepare_cols",
+    "mfb_plan_multiply_cols", "mfb_plan_set_sm_limit",
     "mfb_plan_tune", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
     "mfb_conv2d_fwd", "mfb_naive_sgemm", "mfb_probe_wait_timeout", "mfb_covariance", "mfb_correlation",
     "mfb_probe_tf32_mma_tflops", "mfb_conv2d_bwd_data", "mfb_conv2d_bwd_filter", "mfb_conv2d_bwd_bias",
@@ -94,6 +95,9 @@ def _declare(lib):
         "mfb_plan_execute": (st, [_vp, _vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_float, _vp]),
         "mfb_plan_prepare": (st, [_vp, _vp, _vp, _vp]),
         "mfb_plan_multiply": (st, [_vp, _vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_float, _vp]),
+        "mfb_plan_prepare_cols": (st, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+        "mfb_plan_multiply_cols": (st, [_vp, _vp, _vp, _vp, ctypes.c_float, ctypes.c_float, _vp, ctypes.c_int,
+                                        ctypes.c_int]),
         "mfb_plan_set_sm_limit": (st, [_vp, ctypes.c_int]),
         "mfb_plan_tune": (st, [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                ctypes.POINTER(ctypes.c_float)]),

@@ -42,13 +42,14 @@ struct SplitJob {
     long long x_batch, p_batch;
     const float* shift;
     int blocks;  // blocks of the launch's x dimension that serve this job
+    long long wcols;  // columns written per plane row (multiple of 4, <= ldp); zeros past `cols`
 };
 
 __device__ __forceinline__ void split_tf32_job(const SplitJob& j, int block, int nblocks) {
     const float* x = j.x + blockIdx.y * j.x_batch;
     float* hi = j.hi + blockIdx.y * j.p_batch;
     float* lo = j.lo != nullptr ? j.lo + blockIdx.y * j.p_batch : nullptr;
-    const long long groups_per_row = j.ldp / 4;
+    const long long groups_per_row = j.wcols / 4;
     const long long total = static_cast<long long>(j.rows) * groups_per_row;
     for (long long idx = block * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<long long>(nblocks) * blockDim.x) {
@@ -356,7 +357,8 @@ mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c,
 
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
-                     int phases, int sm_limit, const TcBatch& batch, const TcPrologue& prologue) {
+                     int phases, int sm_limit, const TcBatch& batch, const TcPrologue& prologue,
+                     const TcColumns& cols) {
     const TcEntry* e = find_kernel(cfg);
     if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 kernel for this tile configuration");
     const int nb = batch.count;
@@ -364,6 +366,13 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     if (nb > 1 && e->pair) return fail(MFB_EUNSUPPORTED, "SM-pair kernels do not take a batch");
     const bool run_prepass = (phases & kPhasePrepare) != 0;
     const bool run_gemm = (phases & kPhaseMultiply) != 0;
+    const int n0 = cols.n0, n1 = cols.n1 < 0 ? d.n : cols.n1;
+    const bool col_range = n0 != 0 || n1 != d.n || cols.b_src != nullptr;
+    if (col_range && (d.trans_b || nb != 1 || n0 < 0 || n0 % 32 != 0 || n1 <= n0 || n1 > d.n ||
+                      (n1 != d.n && n1 % 32 != 0)))
+        return fail(MFB_EINVAL,
+                    "column range needs a non-transposed B, one GEMM and 0 <= n0 < n1 <= n, n0 and n1 (unless n) "
+                    "multiples of 32");
 
     // --- operand preparation: hi/lo planes (strict) or one rounded plane (TF32), laid out
     // [plane][batch entry][rows][cols rounded up to 4]. In the prepare-only phase a null
@@ -390,10 +399,19 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         const long long total_groups = static_cast<long long>(op.rows) * (ldp / 4);
         const int blocks = static_cast<int>(
             std::min<long long>((total_groups + 255) / 256, std::max(1LL, 148LL * 8 / nb)));
-        const bool vec = ld % 4 == 0 && src_batch % 4 == 0 && aligned16(src);
-        if (run_prepass && src != nullptr)
-            jobs[which] = SplitJob{src, ld, op.rows, op.cols, hi, lo, ldp, vec ? 1 : 0, src_batch,
-                                   static_cast<long long>(pf), shift, blocks};
+        if (which == 1 && cols.b_src != nullptr) {
+            // columns [n0, n1) of B from a separate matrix, into the same columns of the planes
+            const bool vec_c = cols.b_ld % 4 == 0 && aligned16(cols.b_src);
+            if (run_prepass)
+                jobs[1] = SplitJob{cols.b_src, cols.b_ld, op.rows, n1 - n0, hi + n0, lo ? lo + n0 : nullptr, ldp,
+                                   vec_c ? 1 : 0, 0, static_cast<long long>(pf), nullptr, blocks,
+                                   round_up(static_cast<long long>(n1 - n0), 4)};
+        } else {
+            const bool vec = ld % 4 == 0 && src_batch % 4 == 0 && aligned16(src);
+            if (run_prepass && src != nullptr)
+                jobs[which] = SplitJob{src, ld, op.rows, op.cols, hi, lo, ldp, vec ? 1 : 0, src_batch,
+                                       static_cast<long long>(pf), shift, blocks, ldp};
+        }
         op.base = hi;
         op.ld = ldp;
         op.plane_stride = cfg.planes == 2 ? static_cast<long long>(pf) * nb : 0;
@@ -422,12 +440,13 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
 
     GemmTcParams p{};
     p.m = d.m;
-    p.n = d.n;
+    p.n = n1;  // the launch's last output column + 1
     p.k = d.k;
     p.num_kb = (d.k + kBK - 1) / kBK;
     const int tile_rows = cfg.pair ? 2 * kTcBM : kTcBM;
     p.tiles_m = (d.m + tile_rows - 1) / tile_rows;
-    p.tiles_n = (d.n + cfg.bn - 1) / cfg.bn;
+    p.tiles_n = (n1 - n0 + cfg.bn - 1) / cfg.bn;
+    p.n_base = n0;
     p.batch = nb;
     p.c_batch_stride = batch.stride_c;
     p.group_m = 16;

@@ -18,6 +18,7 @@ struct GemmTcParams {
     int m, n, k;
     int num_kb;          // ceil(k / 32)
     int tiles_m, tiles_n;
+    int n_base;          // first output column of the launch (column-range multiplies), else 0
     int batch;           // strided-batched GEMMs: tiles of batch entry b follow those of b - 1
     long long c_batch_stride;  // floats between consecutive C matrices
     int group_m;         // tile raster: group_m tile-rows walk N together
@@ -57,7 +58,7 @@ struct GemmProblem {
         const int first_m = group * p.group_m;
         const int gsize = min(p.group_m, p.tiles_m - first_m);
         const int in_group = t - group * per_group;
-        return Tile{(first_m + in_group % gsize) * kTcBM, (in_group / gsize) * BN, b};
+        return Tile{(first_m + in_group % gsize) * kTcBM, p.n_base + (in_group / gsize) * BN, b};
     }
 
     __device__ static int valid_cols(const Params& p, const Tile& t) { return min(BN, p.n - t.n0); }

@@ -435,6 +435,52 @@ MFB_API mfb_status_t mfb_plan_multiply(mfb_plan_t plan, mfb_stream_t stream_h, c
     return plan_run(plan, stream_h, a, b, c, alpha, beta, bias, kPhaseMultiply);
 }
 
+MFB_API mfb_status_t mfb_plan_prepare_cols(mfb_plan_t plan, mfb_stream_t stream_h, const float* b, int ldb_src,
+                                           int n0, int n1) {
+    clear_error();
+    if (!plan) return fail(MFB_EINVAL, "Cannot execute a null or destroyed GEMM plan");
+    const mfb_gemm_desc& d = plan->desc;
+    if (plan->path != kPathTc) return fail(MFB_EUNSUPPORTED, "column-range calls need a plan on the tcgen05 path");
+    if (d.trans_b) return fail(MFB_EUNSUPPORTED, "column-range calls need a non-transposed B");
+    if (n0 < 0 || n1 <= n0 || n1 > d.n || n0 % 32 != 0 || (n1 != d.n && n1 % 32 != 0))
+        return fail(MFB_EINVAL, "column range must satisfy 0 <= n0 < n1 <= n with n0 and n1 (unless n) multiples "
+                                "of 32");
+    if (!b || ldb_src < n1 - n0) return fail(MFB_EINVAL, "B column block needs a pointer and ldb >= n1 - n0");
+    DeviceGuard guard;
+    MFB_TRY(select_device(plan->device));
+    TcColumns cols;
+    cols.n0 = n0;
+    cols.n1 = n1;
+    cols.b_src = b;
+    cols.b_ld = ldb_src;
+    return tc_gemm(d, plan->cfg, reinterpret_cast<cudaStream_t>(stream_h), nullptr, nullptr, nullptr, nullptr,
+                   plan->ws, plan->ws_bytes, kPhasePrepare, plan->sm_limit, TcBatch(), TcPrologue(), cols);
+}
+
+MFB_API mfb_status_t mfb_plan_multiply_cols(mfb_plan_t plan, mfb_stream_t stream_h, const float* a, float* c,
+                                            float alpha, float beta, const float* bias, int n0, int n1) {
+    clear_error();
+    if (!plan) return fail(MFB_EINVAL, "Cannot execute a null or destroyed GEMM plan");
+    mfb_gemm_desc d = plan->desc;
+    d.alpha = alpha;
+    d.beta = beta;
+    if (plan->path != kPathTc) return fail(MFB_EUNSUPPORTED, "column-range calls need a plan on the tcgen05 path");
+    if (d.trans_b) return fail(MFB_EUNSUPPORTED, "column-range calls need a non-transposed B");
+    if (n0 < 0 || n1 <= n0 || n1 > d.n || n0 % 32 != 0 || (n1 != d.n && n1 % 32 != 0))
+        return fail(MFB_EINVAL, "column range must satisfy 0 <= n0 < n1 <= n with n0 and n1 (unless n) multiples "
+                                "of 32");
+    if (!a || !c) return fail(MFB_EINVAL, "null A or C pointer");
+    if (c == a) return fail(MFB_EINVAL, "GEMM output cannot alias an input");
+    if (d.epilogue != MFB_EPILOGUE_NONE && !bias) return fail(MFB_ESHAPE, "GEMM bias length must equal N");
+    DeviceGuard guard;
+    MFB_TRY(select_device(plan->device));
+    TcColumns cols;
+    cols.n0 = n0;
+    cols.n1 = n1;
+    return tc_gemm(d, plan->cfg, reinterpret_cast<cudaStream_t>(stream_h), a, nullptr, c, bias, plan->ws,
+                   plan->ws_bytes, kPhaseMultiply, plan->sm_limit, TcBatch(), TcPrologue(), cols);
+}
+
 MFB_API mfb_status_t mfb_plan_set_sm_limit(mfb_plan_t plan, int sms) {
     clear_error();
     if (!plan) return fail(MFB_EINVAL, "null plan");

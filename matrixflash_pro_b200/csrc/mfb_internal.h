@@ -79,6 +79,17 @@ struct TcPrologue {
     const float* b_col_shift = nullptr;
 };
 
+// Column range [n0, n1) of a non-transposed B (n1 < 0: up to n). The prepare phase then
+// splits B's columns [n0, n1) from `b_src` (k x (n1 - n0), row stride b_ld) into the
+// planes' columns [n0, n1); the multiply phase computes only C's columns [n0, n1).
+// n0 is a multiple of 32.
+struct TcColumns {
+    int n0 = 0;
+    int n1 = -1;
+    const float* b_src = nullptr;
+    long long b_ld = 0;
+};
+
 // Tile configurations for `d`, best first. A batch of more than one GEMM uses the
 // single-CTA kernels only.
 int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch = 1);
@@ -94,7 +105,7 @@ enum { kPhasePrepare = 1, kPhaseMultiply = 2, kPhaseAll = 3 };
 mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t stream, const float* a,
                      const float* b, float* c, const float* bias, void* workspace, size_t workspace_bytes,
                      int phases = kPhaseAll, int sm_limit = 0, const TcBatch& batch = TcBatch(),
-                     const TcPrologue& prologue = TcPrologue());
+                     const TcPrologue& prologue = TcPrologue(), const TcColumns& cols = TcColumns());
 
 // cuTensorMapEncodeTiled for FP32 tensors of rank <= 5 (no interleave, L2 256B promotion,
 // zero fill out of bounds); strides_bytes has rank - 1 entries.

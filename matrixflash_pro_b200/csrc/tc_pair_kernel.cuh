@@ -51,7 +51,7 @@ struct GemmPairProblem {
         const int first_m = group * p.group_m;
         const int gsize = min(p.group_m, p.tiles_m - first_m);
         const int in_group = t - group * per_group;
-        return Tile{(first_m + in_group % gsize) * kPairBM, (in_group / gsize) * BN};
+        return Tile{(first_m + in_group % gsize) * kPairBM, p.n_base + (in_group / gsize) * BN};
     }
 
     __device__ static void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile, uint8_t* b_tile,

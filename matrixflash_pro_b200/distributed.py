@@ -1,13 +1,15 @@
 """Row-split multi-GPU GEMM: C = alpha * A * B + beta * C over P ranks (one process per GPU).
 
 Rank r owns rows [r*m/P, (r+1)*m/P) of A and C; B (k x n) lives on rank 0 and reaches
-every rank by an NCCL broadcast over NVLink/NVSwitch. The broadcast is issued in K
-panels (rows of B) on NCCL's stream; the GEMM runs panel by panel as
-C = alpha * A[:, panel] * B[panel, :] + beta' * C (beta' = beta for the first panel,
-1 afterwards), each panel waiting only for its own broadcast, so the transfer of
-panel i+1 overlaps the GEMM of panel i. While later panels are still in flight the
-GEMM runs on a capped grid so NCCL keeps SMs to run on. No output collective: C
-stays row-sharded.
+every rank by NCCL broadcasts over NVLink/NVSwitch. B travels in column panels: rank 0
+packs each panel B[:, n0:n1] into a contiguous k x (n1 - n0) buffer and broadcasts it on
+NCCL's stream. Every rank splits A once per step while the panels are in flight, then per
+panel waits for that panel only, splits it into the plan's B planes (its columns) and
+computes C[:, n0:n1] = alpha * A * B[:, n0:n1] + beta * C[:, n0:n1] on the tcgen05 plan.
+Each column of C is written once (a split along K would read and write all of C once per
+panel), so the first panel, whose broadcast is the only exposed transfer, can be small.
+While later panels are still in flight the GEMM runs on a capped grid so NCCL keeps SMs
+to run on. No output collective: C stays row-sharded.
 
 The reference's precedent is the CPU/GPU row split of HeterogeneousScheduler
 (src/hw/scheduler.cpp:182-312), whose B transfer is host-staged
@@ -18,7 +20,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
-from typing import Callable, List, Optional, Sequence, Tuple
+from typing import Callable, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -37,77 +39,126 @@ def row_partition(m: int, world: int, rank: int) -> Tuple[int, int]:
     return begin, min(m, begin + per)
 
 
-def k_panels(k: int, world: int, first_fraction: float = 0.125, align: int = 32) -> List[Tuple[int, int]]:
-    """K panels for the broadcast/GEMM pipeline: one small leading panel (its broadcast is
-    the only exposed transfer) and one panel for the rest. A single panel without peers."""
-    if world <= 1 or k <= 2 * align:
-        return [(0, k)]
-    first = max(align, int(k * first_fraction) // align * align)
-    if first >= k:
-        return [(0, k)]
-    return [(0, first), (first, k)]
-
-
-PanelGemm = Callable[[int, Tuple[int, int], float, Optional[int]], None]
+def col_panels(n: int, world: int, first_fraction: float = 0.1, tile: int = 256) -> List[Tuple[int, int]]:
+    """Column panels for the broadcast/GEMM pipeline: one small leading panel of whole
+    256-column tiles (its broadcast is the only exposed transfer) and one panel for the rest.
+    A single panel without peers. Measured on 2 B200s with the linear layer (n = 11008): a
+    1024-column first panel whose GEMM leaves 32 SMs to NCCL gave the shortest step; 512 and
+    2048 columns, 16 SMs, or no split at all were slower (NCCL's broadcast occupies more than
+    16 SMs, so a grid of 132 SMs no longer fits beside it and needs an extra wave)."""
+    if world <= 1 or n <= 2 * tile:
+        return [(0, n)]
+    first = max(tile, int(n * first_fraction) // tile * tile)
+    if first >= n:
+        return [(0, n)]
+    return [(0, first), (first, n)]
 
 
 @dataclass
 class PanelSchedule:
     """What one step does, in order: broadcast every panel, then per panel wait + GEMM."""
     panels: List[Tuple[int, int]]
-    betas: List[float]
     sm_limits: List[Optional[int]]
 
 
-def schedule(k: int, world: int, beta: float, comm_sms: int, total_sms: int) -> PanelSchedule:
-    panels = k_panels(k, world)
-    betas = [beta] + [1.0] * (len(panels) - 1)
+def schedule(n: int, world: int, comm_sms: int, total_sms: int) -> PanelSchedule:
+    panels = col_panels(n, world)
     # While later panels are still broadcasting, leave comm_sms SMs to NCCL.
     limits = [max(1, total_sms - comm_sms) if i < len(panels) - 1 else None for i in range(len(panels))]
-    return PanelSchedule(panels, betas, limits)
+    return PanelSchedule(panels, limits)
 
 
-def run_schedule(sched: PanelSchedule, b_rows: Callable[[int, int], torch.Tensor], panel_gemm: PanelGemm,
-                 group=None, src: int = 0,
-                 before_wait: Optional[Callable[[int, Tuple[int, int]], None]] = None) -> None:
-    """Issues the broadcasts (async, NCCL stream), then `before_wait(i, panel)` for every
-    panel (work that does not read B, e.g. preparing A), then the per-panel GEMMs (current
-    stream). `b_rows(k0, k1)` returns the contiguous row block of B's storage for a panel."""
+def run_schedule(sched: PanelSchedule, panel_buffer: Callable[[int], torch.Tensor],
+                 pack_panel: Callable[[int, Tuple[int, int]], None],
+                 panel_gemm: Callable[[int, Tuple[int, int], Optional[int]], None],
+                 group=None, src: int = 0, before_wait: Optional[Callable[[], None]] = None,
+                 prepare_panel: Optional[Callable[[int, Tuple[int, int]], None]] = None,
+                 side: Optional["torch.cuda.Stream"] = None) -> None:
+    """On `src`, `pack_panel(i, panel)` fills panel_buffer(i) before its broadcast; packs and
+    broadcasts are issued from the `side` stream when one is given (NCCL's stream waits for
+    it), so the current stream goes straight on to `before_wait()` (work that does not read
+    B, e.g. preparing A). Then per panel the current stream waits for that panel's broadcast
+    only and runs `panel_gemm(i, panel, sm_limit)`. With `prepare_panel`, panels after the
+    first are prepared on `side` as soon as they arrive (overlapping the previous panel's
+    GEMM) and panel_gemm waits for that instead."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    main = torch.cuda.current_stream() if side is not None else None
+    if side is not None:
+        side.wait_stream(main)  # B (and the panel buffers) as the caller's stream left them
     works = []
-    if world > 1:
-        for (k0, k1) in sched.panels:
-            works.append(dist.broadcast(b_rows(k0, k1), src=src, group=group, async_op=True))
-    if before_wait is not None:
+    with torch.cuda.stream(side) if side is not None else _nullcontext():
         for i, panel in enumerate(sched.panels):
-            before_wait(i, panel)
+            if rank == src:
+                pack_panel(i, panel)
+            if world > 1:
+                works.append(dist.broadcast(panel_buffer(i), src=src, group=group, async_op=True))
+    if before_wait is not None:
+        before_wait()
+    ready = [None] * len(sched.panels)
+    if prepare_panel is not None and side is not None:
+        with torch.cuda.stream(side):
+            for i, panel in enumerate(sched.panels):
+                if i == 0:
+                    continue
+                if works:
+                    works[i].wait()  # side stream waits for this panel's broadcast
+                prepare_panel(i, panel)
+                ev = torch.cuda.Event()
+                ev.record(side)
+                ready[i] = ev
     for i, panel in enumerate(sched.panels):
-        if works:
-            works[i].wait()  # current stream waits for this panel's broadcast only
-        panel_gemm(i, panel, sched.betas[i], sched.sm_limits[i])
+        if ready[i] is not None:
+            main.wait_event(ready[i])
+        else:
+            if works:
+                works[i].wait()  # current stream waits for this panel's broadcast only
+            if prepare_panel is not None:
+                prepare_panel(i, panel)
+        panel_gemm(i, panel, sched.sm_limits[i])
+    if side is not None:
+        main.wait_stream(side)  # nothing of the step is left behind on the side stream
+
+
+class _nullcontext:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
 
 
 class _PointerPlan:
-    """An mfb plan over explicit leading dimensions (panel views of padded operands)."""
+    """An mfb plan over explicit leading dimensions."""
 
     def __init__(self, device: int, m: int, n: int, k: int, lda: int, ldb: int, ldc: int, precision: int):
         self.desc = make_desc(m, n, k, lda, ldb, ldc, 1.0, 0.0, precision)
         h = ctypes.c_void_p()
-        _lib.check(_lib.lib().mfb_plan_create(device, ctypes.byref(self.desc), ctypes.byref(h)), "panel plan")
+        _lib.check(_lib.lib().mfb_plan_create(device, ctypes.byref(self.desc), ctypes.byref(h)), "row-split plan")
         self.handle = h
         self.sm_limit = 0
+        info = _lib.PlanInfo()
+        _lib.check(_lib.lib().mfb_plan_info_get(h, ctypes.byref(info)), "row-split plan info")
+        self.tcgen05 = info.path == 0
 
     def set_sm_limit(self, sms: Optional[int]) -> None:
         sms = int(sms or 0)
         if sms != self.sm_limit:
-            _lib.check(_lib.lib().mfb_plan_set_sm_limit(self.handle, sms), "panel plan sm limit")
+            _lib.check(_lib.lib().mfb_plan_set_sm_limit(self.handle, sms), "plan sm limit")
             self.sm_limit = sms
 
     def prepare(self, stream: int, a: int, b: int) -> None:
-        _lib.check(_lib.lib().mfb_plan_prepare(self.handle, stream, a, b), "panel prepare")
+        _lib.check(_lib.lib().mfb_plan_prepare(self.handle, stream, a, b), "plan prepare")
+
+    def prepare_cols(self, stream: int, b: int, ldb: int, n0: int, n1: int) -> None:
+        _lib.check(_lib.lib().mfb_plan_prepare_cols(self.handle, stream, b, ldb, n0, n1), "plan prepare columns")
 
     def multiply(self, stream: int, a: int, b: int, c: int, alpha: float, beta: float) -> None:
-        _lib.check(_lib.lib().mfb_plan_multiply(self.handle, stream, a, b, c, alpha, beta, 0), "panel multiply")
+        _lib.check(_lib.lib().mfb_plan_multiply(self.handle, stream, a, b, c, alpha, beta, 0), "plan multiply")
+
+    def multiply_cols(self, stream: int, a: int, c: int, alpha: float, beta: float, n0: int, n1: int) -> None:
+        _lib.check(_lib.lib().mfb_plan_multiply_cols(self.handle, stream, a, c, alpha, beta, 0, n0, n1),
+                   "plan multiply columns")
 
     def close(self) -> None:
         if self.handle is not None and self.handle.value:
@@ -125,70 +176,102 @@ class RowSplitGemm:
     """This rank's share of a row-split strict-FP32 (or TF32) GEMM with B broadcast.
 
     A_local: (m_local x k) view of an (m_local x lda) buffer; B: (k x n) view of a
-    (k x ldb) buffer, valid on `src` and overwritten by the broadcast elsewhere;
-    C_local: (m_local x n) view of an (m_local x ldc) buffer."""
+    (k x ldb) buffer, read on `src` (other ranks' B is not touched: the panels arrive in
+    the object's own buffers); C_local: (m_local x n) view of an (m_local x ldc) buffer."""
 
     def __init__(self, m_local: int, n: int, k: int, lda: int, ldb: int, ldc: int,
-                 precision: GemmPrecision = GemmPrecision.fp32, group=None, src: int = 0, comm_sms: int = 16):
+                 precision: GemmPrecision = GemmPrecision.fp32, group=None, src: int = 0, comm_sms: int = 32):
         self.device = torch.cuda.current_device()
         self.group, self.src = group, src
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.m, self.n, self.k = m_local, n, k
         self.lda, self.ldb, self.ldc = lda, ldb, ldc
         total_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self.sched = schedule(k, self.world, 0.0, comm_sms, total_sms)
-        self.plans = [_PointerPlan(self.device, m_local, n, k1 - k0, lda, ldb, ldc, int(precision))
-                      for (k0, k1) in self.sched.panels]
-        # Per-panel GEMM kernel time of the last step, when events are requested.
+        self.plan = _PointerPlan(self.device, m_local, n, k, lda, ldb, ldc, int(precision))
+        self.plans = [self.plan]
+        self.sched = schedule(n, self.world if self.plan.tcgen05 else 1, comm_sms, total_sms)
+        # Contiguous column panels of B, the broadcast buffers (several ranks only).
+        self.panel_bufs: List[torch.Tensor] = []
+        self.side = torch.cuda.Stream(self.device) if self.world > 1 else None
+        if self.world > 1 and self.plan.tcgen05:
+            self.panel_bufs = [torch.empty((k, n1 - n0), dtype=torch.float32, device=self.device)
+                               for (n0, n1) in self.sched.panels]
+        # GEMM kernel time of the last step per panel, when events are requested.
         self.kernel_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
 
     def __call__(self, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, alpha: float = 1.0, beta: float = 0.0,
                  time_kernels: bool = False) -> None:
         stream = _stream_handle()
         a0, b0, c0 = A.data_ptr(), B.data_ptr(), C.data_ptr()
-        sched = PanelSchedule(self.sched.panels, [beta] + [1.0] * (len(self.sched.panels) - 1), self.sched.sm_limits)
         self.kernel_events = []
+        plan = self.plan
 
-        split_a_early = self.world > 1
-
-        def prepare_a(i, panel):
-            # A's split/rounding prepass does not read B: it runs while B is in flight.
-            self.plans[i].prepare(stream, a0 + 4 * panel[0], 0)
-
-        def panel_gemm(i, panel, pbeta, sm_limit):
-            k0, _ = panel
-            plan = self.plans[i]
-            a_ptr = a0 + 4 * k0
-            b_ptr = b0 + 4 * k0 * self.ldb
-            # one prepass launch for both operands unless A's was issued during the broadcast
-            plan.prepare(stream, 0 if split_a_early else a_ptr, b_ptr)
-            plan.set_sm_limit(sm_limit)
+        def timed(fn):
             if time_kernels:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-            plan.multiply(stream, a_ptr, b_ptr, c0, alpha, pbeta)
-            if time_kernels:
+                fn()
                 e1.record()
                 self.kernel_events.append((e0, e1))
+            else:
+                fn()
 
-        def b_rows(k0, k1):
-            return B.as_strided((k1 - k0, self.ldb), (self.ldb, 1), B.storage_offset() + k0 * self.ldb)
+        if self.world == 1:
+            # one prepass launch for both operands, then the GEMM
+            plan.prepare(stream, a0, b0)
+            plan.set_sm_limit(None)
+            timed(lambda: plan.multiply(stream, a0, b0, c0, alpha, beta))
+            return
+        if not plan.tcgen05:
+            # GEMV / scale plans: B's whole (k x ldb) storage is broadcast in place (it is
+            # overwritten on the other ranks), then the plan runs as on one GPU.
+            storage = B.as_strided((self.k, self.ldb), (self.ldb, 1), B.storage_offset())
+            run_schedule(self.sched, lambda i: storage, lambda i, p: None,
+                         lambda i, p, lim: timed(lambda: plan.multiply(stream, a0, b0, c0, alpha, beta)),
+                         self.group, self.src)
+            return
 
-        run_schedule(sched, b_rows, panel_gemm, self.group, self.src,
-                     before_wait=prepare_a if split_a_early else None)
+        def pack(i, panel):
+            n0, n1 = panel
+            self.panel_bufs[i].copy_(B[:, n0:n1])
+
+        def prepare_a():
+            # A's split/rounding prepass does not read B: it runs while B is in flight.
+            plan.prepare(stream, a0, 0)
+
+        def prepare_panel(i, panel):
+            # the panel's B prepass, on whichever stream is current (the side stream for
+            # panels after the first: it overlaps the previous panel's GEMM)
+            n0, n1 = panel
+            plan.prepare_cols(_stream_handle(), self.panel_bufs[i].data_ptr(), n1 - n0, n0, n1)
+
+        def panel_gemm(i, panel, sm_limit):
+            n0, n1 = panel
+            plan.set_sm_limit(sm_limit)
+            timed(lambda: plan.multiply_cols(stream, a0, c0, alpha, beta, n0, n1))
+
+        run_schedule(self.sched, lambda i: self.panel_bufs[i], pack, panel_gemm, self.group, self.src,
+                     before_wait=prepare_a, prepare_panel=prepare_panel, side=self.side)
 
     def launches_per_step(self) -> int:
-        """Kernels of this library per step, per panel: the operand prepass (hi/lo split, or TF32
-        rounding; A's separately while B is broadcast) and the GEMM."""
-        return (3 if self.world > 1 else 2) * len(self.plans)
+        """Kernels of this library per step: on one GPU the operand prepass (hi/lo split, or TF32
+        rounding) and the GEMM; with peers A's prepass, then per column panel its B prepass and
+        its GEMM (the panel packing on rank 0 is a torch copy)."""
+        if self.world == 1 or not self.plan.tcgen05:
+            return 2
+        return 1 + 2 * len(self.sched.panels)
+
+    def gemm_launches_per_step(self) -> int:
+        """GEMM kernels per step (one per column panel)."""
+        return len(self.sched.panels)
 
     def kernel_ms(self) -> float:
         return sum(e0.elapsed_time(e1) for (e0, e1) in self.kernel_events)
 
     def panel_flops(self) -> List[float]:
-        return [2.0 * self.m * self.n * (k1 - k0) for (k0, k1) in self.sched.panels]
+        return [2.0 * self.m * (n1 - n0) * self.k for (n0, n1) in self.sched.panels]
 
     def close(self) -> None:
-        for p in self.plans:
-            p.close()
+        self.plan.close()
         self.plans = []

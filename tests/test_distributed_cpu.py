@@ -1,8 +1,8 @@
 """CPU tier: the multi-GPU row split on 2 gloo ranks (no GPU).
 
-Checks the host logic of matrixflash_pro_b200.distributed: row partition, K panels,
-the broadcast of B panels from rank 0, and the per-panel accumulation rule
-(beta on the first panel, 1 afterwards). The per-panel GEMM is the oracle here (test
+Checks the host logic of matrixflash_pro_b200.distributed: row partition, column panels,
+the packing and broadcast of B's column panels from rank 0, and that each panel's GEMM
+writes its own columns of C. The per-panel GEMM is the oracle here (test
 infrastructure), standing in for the tcgen05 plan that runs on the GPU."""
 import os
 import socket
@@ -13,7 +13,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from matrixflash_pro_b200.distributed import k_panels, row_partition, run_schedule, schedule
+from matrixflash_pro_b200.distributed import col_panels, row_partition, run_schedule, schedule
 
 
 def test_row_partition_covers_rows_once():
@@ -27,21 +27,21 @@ def test_row_partition_covers_rows_once():
         row_partition(10, 2, 2)
 
 
-def test_k_panels():
-    assert k_panels(4096, 1) == [(0, 4096)]
-    assert k_panels(4096, 8) == [(0, 512), (512, 4096)]
-    assert k_panels(32768, 2) == [(0, 4096), (4096, 32768)]
-    assert k_panels(40, 4) == [(0, 40)]
-    for k in (100, 4097, 5000):
-        p = k_panels(k, 4)
-        assert p[0][0] == 0 and p[-1][1] == k and all(a < b for a, b in p) and p[0][1] % 32 == 0
+def test_col_panels():
+    assert col_panels(11008, 1) == [(0, 11008)]
+    assert col_panels(11008, 8) == [(0, 1024), (1024, 11008)]
+    assert col_panels(32768, 2) == [(0, 3072), (3072, 32768)]
+    assert col_panels(300, 4) == [(0, 300)]
+    for n in (600, 4097, 5000):
+        p = col_panels(n, 4)
+        assert p[0][0] == 0 and p[-1][1] == n and all(a < b for a, b in p) and p[0][1] % 256 == 0
 
 
-def test_schedule_betas_and_sm_limits():
-    s = schedule(4096, 4, 0.5, 16, 148)
-    assert s.betas == [0.5, 1.0] and s.sm_limits == [132, None]
-    s1 = schedule(4096, 1, 0.5, 16, 148)
-    assert s1.betas == [0.5] and s1.sm_limits == [None]
+def test_schedule_sm_limits():
+    s = schedule(11008, 4, 32, 148)
+    assert s.sm_limits == [116, None] and len(s.panels) == 2
+    s1 = schedule(11008, 1, 16, 148)
+    assert s1.panels == [(0, 11008)] and s1.sm_limits == [None]
 
 
 def _free_port():
@@ -57,7 +57,7 @@ def _worker(rank, world, port, result_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        m, n, k, ldb = 37, 29, 300, 31
+        m, n, k, ldb = 37, 600, 70, 611
         alpha, beta = 0.5, 1.0
         rng = np.random.default_rng(0)
         A_full = rng.uniform(-1, 1, (m, k)).astype(np.float32)
@@ -67,17 +67,23 @@ def _worker(rank, world, port, result_dir):
         A = A_full[r0:r1].copy()
         C = C_full[r0:r1].copy()
         B = torch.from_numpy(B_full.copy()) if rank == 0 else torch.full((k, ldb), float("nan"))
-        sched = schedule(k, world, beta, 16, 148)
+        sched = schedule(n, world, 16, 148)
+        assert len(sched.panels) == 2
+        bufs = [torch.full((k, n1 - n0), float("nan")) for (n0, n1) in sched.panels]
 
-        def panel_gemm(i, panel, pbeta, sm_limit):
-            k0, k1 = panel
-            b_panel = B[k0:k1].numpy()
-            a_panel = np.ascontiguousarray(A[:, k0:k1])
-            oracle.gemm_f32(r1 - r0, n, k1 - k0, a_panel, k1 - k0, b_panel, ldb, C, n, alpha, pbeta)
+        def pack(i, panel):
+            n0, n1 = panel
+            bufs[i].copy_(B[:, n0:n1])
 
-        run_schedule(sched, lambda k0, k1: B[k0:k1], panel_gemm)
+        def panel_gemm(i, panel, sm_limit):
+            n0, n1 = panel
+            cp = np.ascontiguousarray(C[:, n0:n1])
+            oracle.gemm_f32(r1 - r0, n1 - n0, k, A, k, bufs[i].numpy(), n1 - n0, cp, n1 - n0, alpha, beta)
+            C[:, n0:n1] = cp
+
+        run_schedule(sched, lambda i: bufs[i], pack, panel_gemm)
         np.save(os.path.join(result_dir, f"c{rank}.npy"), C)
-        np.save(os.path.join(result_dir, f"b{rank}.npy"), B.numpy())
+        np.save(os.path.join(result_dir, f"b{rank}.npy"), np.concatenate([b.numpy() for b in bufs], axis=1))
     finally:
         dist.destroy_process_group()
 
@@ -86,14 +92,14 @@ def test_row_split_with_panel_broadcast_two_gloo_ranks(tmp_path):
     world = 2
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
     import oracle
-    m, n, k, ldb = 37, 29, 300, 31
+    m, n, k, ldb = 37, 600, 70, 611
     rng = np.random.default_rng(0)
     A_full = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     B_full = rng.standard_normal((k, ldb)).astype(np.float32)
     C_full = rng.standard_normal((m, n)).astype(np.float32)
     got = np.concatenate([np.load(tmp_path / f"c{r}.npy") for r in range(world)])
     for r in range(world):
-        assert np.array_equal(np.load(tmp_path / f"b{r}.npy"), B_full), "B reached every rank"
+        assert np.array_equal(np.load(tmp_path / f"b{r}.npy"), B_full[:, :n]), "B's panels reached every rank"
     ref64 = 0.5 * (A_full.astype(np.float64) @ B_full[:, :n].astype(np.float64)) + C_full
     ref32 = C_full.copy()
     oracle.gemm_f32(m, n, k, A_full, k, B_full, ldb, ref32, n, 0.5, 1.0)

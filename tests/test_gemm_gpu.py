@@ -328,3 +328,33 @@ def test_tf32_mma_rate_probe():
     assert mf.device_status() == 0
     with pytest.raises(mf.InvalidArgumentError):
         mf.probe_tf32_mma_tflops(96)
+
+
+@pytest.mark.parametrize("precision", [FP32, TF32])
+def test_column_range_phases_equal_execute(precision):
+    """mfb_plan_prepare_cols / mfb_plan_multiply_cols (B arriving in contiguous column panels,
+    as the row split broadcasts it) give the bits of one mfb_plan_execute."""
+    from matrixflash_pro_b200 import _lib
+    from matrixflash_pro_b200.gemm import _stream_handle
+    m, n, k = 1000, 2000, 700
+    g = torch.Generator(device="cuda").manual_seed(12)
+    A = torch.randn((m, k), device="cuda", generator=g)
+    B = torch.randn((k, n), device="cuda", generator=g)
+    C0 = torch.randn((m, n), device="cuda", generator=g)
+    p = mf.GemmPlan(m, n, k, mf.GemmOptions(precision=precision))
+    want = C0.clone()
+    p.execute(A, B, want, 0.5, 1.0)
+    lib, h, s = _lib.lib(), p._handle, _stream_handle()
+    got = C0.clone()
+    _lib.check(lib.mfb_plan_prepare(h, s, A.data_ptr(), 0), "prepare A")
+    for n0, n1 in [(512, 2000), (0, 512)]:
+        Bp = B[:, n0:n1].contiguous()
+        _lib.check(lib.mfb_plan_prepare_cols(h, s, Bp.data_ptr(), n1 - n0, n0, n1), "prepare cols")
+        _lib.check(lib.mfb_plan_multiply_cols(h, s, A.data_ptr(), got.data_ptr(), 0.5, 1.0, 0, n0, n1),
+                   "multiply cols")
+        mf.sync()  # Bp is freed at the end of the iteration
+    assert torch.equal(got, want)
+    with pytest.raises(mf.InvalidArgumentError):
+        _lib.check(lib.mfb_plan_multiply_cols(h, s, A.data_ptr(), got.data_ptr(), 1.0, 0.0, 0, 16, 64), "n0")
+    with pytest.raises(mf.InvalidArgumentError):
+        _lib.check(lib.mfb_plan_prepare_cols(h, s, B.data_ptr(), n, 0, n + 32), "n1")
