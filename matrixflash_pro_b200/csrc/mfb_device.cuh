@@ -297,6 +297,15 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// After tmem_ld_wait: redefines the registers of one x16 load in an (empty) volatile asm, so
+// no use of them can be scheduled above the wait when several loads share one wait.
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[16]) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]));
+}
+
 // ----------------------------------------------------------------------------------------
 // UMMA shared-memory matrix descriptors (sm_100 format: version 1 at bits 46-47).
 // ----------------------------------------------------------------------------------------

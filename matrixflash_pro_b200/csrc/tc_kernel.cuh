@@ -128,6 +128,26 @@ __device__ __forceinline__ void tc_epilogue_role(const typename Prob::Params& p,
                     break;
                 }
                 tc_fence_after();
+                if constexpr (Prob::kStackB && kStep == 16 && kCols <= 32) {
+                    // Narrow stacked tiles: all loads of the chunk (both halves) in flight at
+                    // once, one wait. The chunk's MMAs are short here, so the epilogue has to
+                    // drain a chunk faster than one TMEM load round trip per 16 columns allows.
+                    uint32_t rh[kCols / 16][16], rl[kCols / 16][16];
+#pragma unroll
+                    for (int q = 0; q < kCols / 16; ++q) {
+                        tmem_ld_32x32b_x16(tmem_base + lane_base + b * ACC + half * kCols + q * 16, rh[q]);
+                        tmem_ld_32x32b_x16(tmem_base + lane_base + b * ACC + BN + half * kCols + q * 16, rl[q]);
+                    }
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int q = 0; q < kCols / 16; ++q) {
+                        tmem_regs_ready(rh[q]);
+                        tmem_regs_ready(rl[q]);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            sum[q * 16 + j] += __uint_as_float(rh[q][j]) + __uint_as_float(rl[q][j]);
+                    }
+                } else
 #pragma unroll
                 for (int q = 0; q < kCols / kStep; ++q) {
                     float v[kStep];
