@@ -182,6 +182,7 @@ typedef struct mfb_plan_info {
     int candidates;        /* tile configurations considered by mfb_plan_tune */
     size_t workspace_bytes;/* device scratch owned by the plan */
     char kernel[64];       /* kernel family name */
+    int sm_pair;           /* 1: 256-row tiles on SM pairs (tcgen05.mma.cta_group::2) */
 } mfb_plan_info;
 
 /* Builds tile choice, scratch and launch state for one problem on `device`.

@@ -48,7 +48,8 @@ class PlanInfo(ctypes.Structure):
     _fields_ = [("m", ctypes.c_int), ("n", ctypes.c_int), ("k", ctypes.c_int), ("precision", ctypes.c_int),
                 ("trans_a", ctypes.c_int), ("trans_b", ctypes.c_int), ("epilogue", ctypes.c_int),
                 ("path", ctypes.c_int), ("tile_n", ctypes.c_int), ("stages", ctypes.c_int),
-                ("candidates", ctypes.c_int), ("workspace_bytes", ctypes.c_size_t), ("kernel", ctypes.c_char * 64)]
+                ("candidates", ctypes.c_int), ("workspace_bytes", ctypes.c_size_t), ("kernel", ctypes.c_char * 64),
+                ("sm_pair", ctypes.c_int)]
 
 
 _vp = ctypes.c_void_p

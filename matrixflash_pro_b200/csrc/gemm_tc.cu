@@ -227,9 +227,15 @@ TcEntry make_pair_entry() {
 
 const TcEntry* kernel_table(int* count) {
     static const TcEntry table[] = {
-        // SM pairs, 256 x 256 tiles: strict and TF32
+        // SM pairs, 256 x 256 tiles: strict and TF32, every transpose combination
         make_pair_entry<256, 3, 2, 0, 1>(),
         make_pair_entry<256, 6, 1, 0, 1>(),
+        make_pair_entry<256, 3, 2, 1, 1>(),
+        make_pair_entry<256, 6, 1, 1, 1>(),
+        make_pair_entry<256, 3, 2, 0, 0>(),
+        make_pair_entry<256, 6, 1, 0, 0>(),
+        make_pair_entry<256, 3, 2, 1, 0>(),
+        make_pair_entry<256, 6, 1, 1, 0>(),
         // strict FP32 (3xTF32 split planes, chunked round-to-nearest accumulation)
         make_entry<256, 2, 2, 0, 1>(),
         make_entry<128, 3, 2, 0, 1>(),
@@ -381,8 +387,21 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     SplitJob jobs[2] = {};
     size_t used = 0;
     char* ws = static_cast<char*>(workspace);
+    if (prologue.shared_planes) {
+        int ra, ca, rb, cb;
+        long long la, lb;
+        stored_dims(d, true, &ra, &ca, &la);
+        stored_dims(d, false, &rb, &cb, &lb);
+        if (a != b || la != lb || ra != rb || ca != cb || prologue.a_col_shift != prologue.b_col_shift ||
+            cols.b_src != nullptr)
+            return fail(MFB_EINVAL, "shared operand planes need A and B to be the same stored matrix");
+    }
     for (int which = 0; which < 2; ++which) {
         PreparedOperand& op = ops[which];
+        if (which == 1 && prologue.shared_planes) {
+            op = ops[0];  // B reads A's planes
+            break;
+        }
         long long ld;
         stored_dims(d, which == 0, &op.rows, &op.cols, &ld);
         const float* src = which == 0 ? a : b;
@@ -434,8 +453,10 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         MFB_TRY(encode_operand(&map_a, A.base, A.rows, A.cols, A.ld, cfg.planes, A.plane_stride, 32,
                                cfg.a_mn ? 32 : kTcBM, cfg.a_mn != 0, !e->pair, nb, A.batch_stride));
         const PreparedOperand& B = ops[1];
-        MFB_TRY(encode_operand(&map_b, B.base, B.rows, B.cols, B.ld, cfg.planes, B.plane_stride, 32,
-                               cfg.b_mn ? 32 : cfg.bn, cfg.b_mn != 0, !e->pair, nb, B.batch_stride));
+        // K-major B: box of the tile's columns, half of them per CTA on SM pairs; MN-major B: 32 x 32.
+        const int b_rows = cfg.b_mn ? 32 : (e->pair ? cfg.bn / 2 : cfg.bn);
+        MFB_TRY(encode_operand(&map_b, B.base, B.rows, B.cols, B.ld, cfg.planes, B.plane_stride, 32, b_rows,
+                               cfg.b_mn != 0, !e->pair, nb, B.batch_stride));
     }
 
     GemmTcParams p{};

@@ -346,7 +346,8 @@ __global__ void __launch_bounds__(128) gemv_cols_partial_kernel(const float* __r
     const int k1 = min(k, k0 + k_per_split);
     if (col >= n) return;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = k0; p < k1; ++p) {
+#pragma unroll 8
+    for (int p = k0; p < k1; ++p) {  // unrolled: eight row loads in flight per thread
         const float xv = __ldg(x + p);
         const float* src = b + static_cast<long long>(p) * ldb + col;
         float4 bv;
@@ -384,8 +385,8 @@ __global__ void gemv_cols_finish_kernel(const float* __restrict__ partial, int s
 // x^T for m == 1 lives in A's single row (lda irrelevant); it must be contiguous.
 int cols_splits(int n, int k) {
     const int col_blocks = (n + 511) / 512;
-    int splits = std::max(1, (148 * 4) / std::max(1, col_blocks));
-    splits = std::min(splits, std::max(1, k / 64));
+    int splits = std::max(1, (148 * 8) / std::max(1, col_blocks));  // ~8 blocks of 4 warps per SM
+    splits = std::min(splits, std::max(1, k / 32));
     return std::min(splits, 1024);
 }
 

@@ -564,6 +564,7 @@ MFB_API mfb_status_t mfb_plan_info_get(mfb_plan_t plan, mfb_plan_info* info) {
                            ? (plan->cfg.planes == 2 ? "tcgen05_3xtf32" : "tcgen05_tf32")
                            : plan->path == kPathGemv ? "gemv_fp32" : plan->path == kPathScale ? "scale" : "empty";
     std::snprintf(info->kernel, sizeof(info->kernel), "%s", name);
+    info->sm_pair = plan->path == kPathTc ? plan->cfg.pair : 0;
     return MFB_OK;
 }
 

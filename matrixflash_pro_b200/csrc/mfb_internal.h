@@ -77,6 +77,9 @@ struct TcBatch {
 struct TcPrologue {
     const float* a_col_shift = nullptr;
     const float* b_col_shift = nullptr;
+    // A and B are the same stored matrix with the same shift (X^T X): one prepass, and both
+    // operand maps read the same planes.
+    bool shared_planes = false;
 };
 
 // Column range [n0, n1) of a non-transposed B (n1 < 0: up to n). The prepare phase then

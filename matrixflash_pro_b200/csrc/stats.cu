@@ -110,6 +110,7 @@ mfb_status_t covariance_run(int device, cudaStream_t stream, int rows, int cols,
     TcPrologue centering;
     centering.a_col_shift = mean;
     centering.b_col_shift = mean;
+    centering.shared_planes = true;  // X^T X: one centered split of X serves both operands
     return tc_gemm(plan.cov_desc, cfgs[0], stream, x, x, target, nullptr, base + plan.tc_off, plan.tc_bytes,
                    kPhaseAll, 0, TcBatch(), centering);
 }

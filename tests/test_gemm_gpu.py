@@ -13,7 +13,7 @@ import torch
 
 import matrixflash_pro_b200 as mf
 import oracle
-from helpers import assert_strict, assert_tf32, to_dev
+from helpers import STRICT_NORMWISE, assert_strict, assert_tf32, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -358,3 +358,25 @@ def test_column_range_phases_equal_execute(precision):
         _lib.check(lib.mfb_plan_multiply_cols(h, s, A.data_ptr(), got.data_ptr(), 1.0, 0.0, 0, 16, 64), "n0")
     with pytest.raises(mf.InvalidArgumentError):
         _lib.check(lib.mfb_plan_prepare_cols(h, s, B.data_ptr(), n, 0, n + 32), "n1")
+
+
+@pytest.mark.parametrize("precision", [FP32, TF32])
+@pytest.mark.parametrize("ta,tb", [(True, True), (False, False), (True, False)])
+def test_sm_pair_transposed_operands(ta, tb, precision):
+    """256 x 256 SM-pair tiles with MN-major A and/or K-major B (2048 x 2048 outputs fill the pairs)."""
+    m, n, k = 2048, 2048, 544
+    g = torch.Generator(device="cuda").manual_seed(31 + 2 * ta + tb)
+    A = torch.randn((k, m) if ta else (m, k), device="cuda", generator=g)
+    B = torch.randn((n, k) if tb else (k, n), device="cuda", generator=g)
+    C0 = torch.randn((m, n), device="cuda", generator=g)
+    o = mf.GemmOptions(precision=precision, transpose_left=ta, transpose_right=tb)
+    p = mf.GemmPlan(m, n, k, o)
+    assert p.info().sm_pair == 1
+    C = C0.clone()
+    p.execute(A, B, C, 0.75, -0.5)
+    mf.sync()
+    Ad = A.double().t() if ta else A.double()
+    Bd = B.double().t() if tb else B.double()
+    ref = 0.75 * (Ad @ Bd) - 0.5 * C0.double()
+    err = float((C.double() - ref).norm() / ref.norm())
+    assert err <= (STRICT_NORMWISE if precision == FP32 else 5e-3), err
