@@ -132,33 +132,24 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Map over a stored row-major matrix (cols contiguous) with an outer plane axis: 3-D
-// (cols, rows, plane) for the SM-pair kernels, 4-D (cols, rows, batch, plane) for the
-// single-CTA kernels. K-major tiles use the 128B swizzle with 16-byte atoms; MN-major
-// TF32 tiles the 128B swizzle with 32-byte atoms, the only shared-memory layout tcgen05
-// accepts for them.
+// Map over a stored row-major matrix (cols contiguous) with outer batch and plane axes:
+// 4-D (cols, rows, batch, plane), for the single-CTA and the SM-pair kernels alike. K-major
+// tiles use the 128B swizzle with 16-byte atoms; MN-major TF32 tiles the 128B swizzle with
+// 32-byte atoms, the only shared-memory layout tcgen05 accepts for them.
 mfb_status_t encode_operand(CUtensorMap* map, const float* base, int rows, int cols, long long ld, int planes,
-                            long long plane_stride_floats, int box_cols, int box_rows, bool mn_major, bool batched,
+                            long long plane_stride_floats, int box_cols, int box_rows, bool mn_major,
                             int batch = 1, long long batch_stride_floats = 0) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return fail(MFB_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
     const long long plane_stride = plane_stride_floats > 0 ? plane_stride_floats : ld * static_cast<long long>(rows);
     const long long batch_stride = batch_stride_floats > 0 ? batch_stride_floats : ld * static_cast<long long>(rows);
-    const int rank = batched ? 4 : 3;
-    cuuint64_t dims[4] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), 0, 0};
-    cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld) * 4, 0, 0};
-    cuuint32_t box[4] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1, 1};
-    if (batched) {
-        dims[2] = static_cast<cuuint64_t>(batch);
-        dims[3] = static_cast<cuuint64_t>(planes);
-        strides[1] = static_cast<cuuint64_t>(batch_stride) * 4;
-        strides[2] = static_cast<cuuint64_t>(plane_stride) * 4;
-        box[3] = static_cast<cuuint32_t>(planes);
-    } else {
-        dims[2] = static_cast<cuuint64_t>(planes);
-        strides[1] = static_cast<cuuint64_t>(plane_stride) * 4;
-        box[2] = static_cast<cuuint32_t>(planes);
-    }
+    const int rank = 4;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(batch), static_cast<cuuint64_t>(planes)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(batch_stride) * 4,
+                             static_cast<cuuint64_t>(plane_stride) * 4};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1,
+                         static_cast<cuuint32_t>(planes)};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<cuuint32_t>(rank), const_cast<float*>(base),
                     dims, strides, box, estr,
@@ -310,7 +301,7 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch)
     int order[16];
     int n_ok = 0;
     for (int i = 0; i < count && n_ok < 16; ++i)
-        if (t[i].planes == planes && t[i].a_mn == a_mn && t[i].b_mn == b_mn && (batch == 1 || !t[i].pair))
+        if (t[i].planes == planes && t[i].a_mn == a_mn && t[i].b_mn == b_mn)
             order[n_ok++] = i;
     // SM pairs first when they fill the GPU (their 256-row tiles halve B's shared-memory
     // traffic per FLOP), then the widest single-CTA tile that fills it, then narrower ones.
@@ -369,7 +360,6 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 kernel for this tile configuration");
     const int nb = batch.count;
     if (nb < 1 || nb > 65535) return fail(MFB_EINVAL, "batch count must be in [1, 65535]");
-    if (nb > 1 && e->pair) return fail(MFB_EUNSUPPORTED, "SM-pair kernels do not take a batch");
     const bool run_prepass = (phases & kPhasePrepare) != 0;
     const bool run_gemm = (phases & kPhaseMultiply) != 0;
     const int n0 = cols.n0, n1 = cols.n1 < 0 ? d.n : cols.n1;
@@ -451,12 +441,12 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         const PreparedOperand& A = ops[0];
         // K-major A: box 32 (K) x 128 (M); MN-major A: box 32 (M) x 32 (K).
         MFB_TRY(encode_operand(&map_a, A.base, A.rows, A.cols, A.ld, cfg.planes, A.plane_stride, 32,
-                               cfg.a_mn ? 32 : kTcBM, cfg.a_mn != 0, !e->pair, nb, A.batch_stride));
+                               cfg.a_mn ? 32 : kTcBM, cfg.a_mn != 0, nb, A.batch_stride));
         const PreparedOperand& B = ops[1];
         // K-major B: box of the tile's columns, half of them per CTA on SM pairs; MN-major B: 32 x 32.
         const int b_rows = cfg.b_mn ? 32 : (e->pair ? cfg.bn / 2 : cfg.bn);
         MFB_TRY(encode_operand(&map_b, B.base, B.rows, B.cols, B.ld, cfg.planes, B.plane_stride, 32, b_rows,
-                               cfg.b_mn != 0, !e->pair, nb, B.batch_stride));
+                               cfg.b_mn != 0, nb, B.batch_stride));
     }
 
     GemmTcParams p{};

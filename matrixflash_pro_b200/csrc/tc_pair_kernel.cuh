@@ -41,17 +41,21 @@ struct GemmPairProblem {
 
     struct Tile {
         int m0, n0;  // pair tile origin (256 x BN)
+        int b;       // batch entry
     };
 
-    __device__ static int num_tiles(const Params& p) { return p.tiles_m * p.tiles_n; }
+    __device__ static int num_tiles(const Params& p) { return p.batch * p.tiles_m * p.tiles_n; }
 
     __device__ static Tile tile(const Params& p, int t) {
+        const int per_batch = p.tiles_m * p.tiles_n;
+        const int b = t / per_batch;
+        t -= b * per_batch;
         const int per_group = p.group_m * p.tiles_n;
         const int group = t / per_group;
         const int first_m = group * p.group_m;
         const int gsize = min(p.group_m, p.tiles_m - first_m);
         const int in_group = t - group * per_group;
-        return Tile{(first_m + in_group % gsize) * kPairBM, p.n_base + (in_group / gsize) * BN};
+        return Tile{(first_m + in_group % gsize) * kPairBM, p.n_base + (in_group / gsize) * BN, b};
     }
 
     __device__ static void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile, uint8_t* b_tile,
@@ -59,19 +63,20 @@ struct GemmPairProblem {
         const int k0 = kb * kBK;
         const int ma = t.m0 + kTcBM * rank;
         const int nb = t.n0 + kBH * rank;
+        // maps are 4-D: (cols, rows, batch entry, plane)
         if (A_MN) {
 #pragma unroll
             for (int g = 0; g < kTcBM / 32; ++g)
-                tma_load_3d_pair(a_tile + g * PLANES * 4096, ta, full_bar_leader, ma + 32 * g, k0, 0);
+                tma_load_4d_pair(a_tile + g * PLANES * 4096, ta, full_bar_leader, ma + 32 * g, k0, t.b, 0);
         } else {
-            tma_load_3d_pair(a_tile, ta, full_bar_leader, k0, ma, 0);
+            tma_load_4d_pair(a_tile, ta, full_bar_leader, k0, ma, t.b, 0);
         }
         if (B_MN) {
 #pragma unroll
             for (int g = 0; g < kBH / 32; ++g)
-                tma_load_3d_pair(b_tile + g * PLANES * 4096, tb, full_bar_leader, nb + 32 * g, k0, 0);
+                tma_load_4d_pair(b_tile + g * PLANES * 4096, tb, full_bar_leader, nb + 32 * g, k0, t.b, 0);
         } else {
-            tma_load_3d_pair(b_tile, tb, full_bar_leader, k0, nb, 0);
+            tma_load_4d_pair(b_tile, tb, full_bar_leader, k0, nb, t.b, 0);
         }
     }
 
@@ -86,7 +91,7 @@ struct GemmPairProblem {
     __device__ static void store(const Params& p, const Tile& t, int rank, int row_in_tile, int col0_in_tile,
                                  const float* v) {
         using One = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>;
-        typename One::Tile ot{t.m0 + kTcBM * rank, t.n0};
+        typename One::Tile ot{t.m0 + kTcBM * rank, t.n0, t.b};
         One::template store<COUNT>(p, ot, row_in_tile, col0_in_tile, v);
     }
 };
