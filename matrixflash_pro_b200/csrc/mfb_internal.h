@@ -93,8 +93,8 @@ struct TcColumns {
     long long b_ld = 0;
 };
 
-// Tile configurations for `d`, best first. A batch of more than one GEMM uses the
-// single-CTA kernels only.
+// Tile configurations for `d`, best first (SM-pair 256 x 256 tiles when they fill the GPU,
+// for single GEMMs and strided batches alike).
 int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch = 1);
 
 // Scratch the tcgen05 path needs for `d`: hi/lo planes of A and B (strict) or one
