@@ -9,3 +9,4 @@
 #include "peak_probe.cu"
 #include "collectives.cu"
 #include "host_gemm.cu"
+#include "plugin.cu"
