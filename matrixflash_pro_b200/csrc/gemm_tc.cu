@@ -198,6 +198,7 @@ struct TcEntry {
     int smem;
     int threads;
     int pair;  // SM-pair kernel (cluster of 2, 256-row tiles)
+    int kslabs;  // 32-deep K slabs per stage (the kernel's K block is 32 * kslabs deep)
 };
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
@@ -205,28 +206,28 @@ TcEntry make_entry() {
     using P = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>;
     using L = TcLayout<P>;
     return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes,
-                   L::kThreads, 0};
+                   L::kThreads, 0, 1};
 }
 
-template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
+template <int BN, int STAGES, int PLANES, int A_MN, int B_MN, int KS = 1>
 TcEntry make_pair_entry() {
-    using P = GemmPairProblem<BN, STAGES, PLANES, A_MN, B_MN>;
+    using P = GemmPairProblem<BN, STAGES, PLANES, A_MN, B_MN, KS>;
     using L = TcPairLayout<P>;
     return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_pair_kernel<P>), L::kBytes,
-                   L::kThreads, 1};
+                   L::kThreads, 1, KS};
 }
 
 const TcEntry* kernel_table(int* count) {
     static const TcEntry table[] = {
         // SM pairs, 256 x 256 tiles: strict and TF32, every transpose combination
         make_pair_entry<256, 3, 2, 0, 1>(),
-        make_pair_entry<256, 6, 1, 0, 1>(),
+        make_pair_entry<256, 3, 1, 0, 1, 2>(),
         make_pair_entry<256, 3, 2, 1, 1>(),
-        make_pair_entry<256, 6, 1, 1, 1>(),
+        make_pair_entry<256, 3, 1, 1, 1, 2>(),
         make_pair_entry<256, 3, 2, 0, 0>(),
-        make_pair_entry<256, 6, 1, 0, 0>(),
+        make_pair_entry<256, 3, 1, 0, 0, 2>(),
         make_pair_entry<256, 3, 2, 1, 0>(),
-        make_pair_entry<256, 6, 1, 1, 0>(),
+        make_pair_entry<256, 3, 1, 1, 0, 2>(),
         // strict FP32 (3xTF32 split planes, chunked round-to-nearest accumulation)
         make_entry<256, 2, 2, 0, 1>(),
         make_entry<128, 3, 2, 0, 1>(),
@@ -453,7 +454,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     p.m = d.m;
     p.n = n1;  // the launch's last output column + 1
     p.k = d.k;
-    p.num_kb = (d.k + kBK - 1) / kBK;
+    p.num_kb = (d.k + kBK * e->kslabs - 1) / (kBK * e->kslabs);
     const int tile_rows = cfg.pair ? 2 * kTcBM : kTcBM;
     p.tiles_m = (d.m + tile_rows - 1) / tile_rows;
     p.tiles_n = (n1 - n0 + cfg.bn - 1) / cfg.bn;

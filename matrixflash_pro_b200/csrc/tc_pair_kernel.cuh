@@ -28,14 +28,20 @@
 
 namespace mfb {
 
-template <int BN_, int STAGES_, int PLANES_, int A_MN_, int B_MN_>
+// KS = 32-deep K slabs per stage (a K block is 32 * KS deep; KS = 2 only for TF32, whose
+// accumulator is not chunked).
+template <int BN_, int STAGES_, int PLANES_, int A_MN_, int B_MN_, int KS_ = 1>
 struct GemmPairProblem {
     using Params = GemmTcParams;
     static constexpr int BN = BN_, STAGES = STAGES_, PLANES = PLANES_, A_MN = A_MN_, B_MN = B_MN_;
+    static constexpr int KS = KS_;
+    static_assert(KS == 1 || PLANES == 1, "strict chunking counts 32-deep K blocks");
     static constexpr int kBH = BN / 2;  // B columns per CTA
-    static constexpr int kATileBytes = PLANES * kTcBM * kBK * 4;
-    static constexpr int kBTileBytes = PLANES * kBH * kBK * 4;
-    static constexpr int kKSteps = kBK / 8;
+    static constexpr int kASlabBytes = PLANES * kTcBM * kBK * 4;
+    static constexpr int kBSlabBytes = PLANES * kBH * kBK * 4;
+    static constexpr int kATileBytes = KS * kASlabBytes;
+    static constexpr int kBTileBytes = KS * kBSlabBytes;
+    static constexpr int kKSteps = KS * kBK / 8;
     static constexpr int kPairBM = 2 * kTcBM;
     static_assert(kBH % 32 == 0 || !B_MN, "MN-major B halves are 32-column groups");
 
@@ -60,31 +66,38 @@ struct GemmPairProblem {
 
     __device__ static void load(const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile, uint8_t* b_tile,
                                 uint32_t full_bar_leader, const Tile& t, int kb, int rank) {
-        const int k0 = kb * kBK;
         const int ma = t.m0 + kTcBM * rank;
         const int nb = t.n0 + kBH * rank;
-        // maps are 4-D: (cols, rows, batch entry, plane)
-        if (A_MN) {
+        // maps are 4-D: (cols, rows, batch entry, plane); slab j of the stage holds K [k0, k0 + 32)
 #pragma unroll
-            for (int g = 0; g < kTcBM / 32; ++g)
-                tma_load_4d_pair(a_tile + g * PLANES * 4096, ta, full_bar_leader, ma + 32 * g, k0, t.b, 0);
-        } else {
-            tma_load_4d_pair(a_tile, ta, full_bar_leader, k0, ma, t.b, 0);
-        }
-        if (B_MN) {
+        for (int j = 0; j < KS; ++j) {
+            const int k0 = (kb * KS + j) * kBK;
+            uint8_t* as = a_tile + j * kASlabBytes;
+            uint8_t* bs = b_tile + j * kBSlabBytes;
+            if (A_MN) {
 #pragma unroll
-            for (int g = 0; g < kBH / 32; ++g)
-                tma_load_4d_pair(b_tile + g * PLANES * 4096, tb, full_bar_leader, nb + 32 * g, k0, t.b, 0);
-        } else {
-            tma_load_4d_pair(b_tile, tb, full_bar_leader, k0, nb, t.b, 0);
+                for (int g = 0; g < kTcBM / 32; ++g)
+                    tma_load_4d_pair(as + g * PLANES * 4096, ta, full_bar_leader, ma + 32 * g, k0, t.b, 0);
+            } else {
+                tma_load_4d_pair(as, ta, full_bar_leader, k0, ma, t.b, 0);
+            }
+            if (B_MN) {
+#pragma unroll
+                for (int g = 0; g < kBH / 32; ++g)
+                    tma_load_4d_pair(bs + g * PLANES * 4096, tb, full_bar_leader, nb + 32 * g, k0, t.b, 0);
+            } else {
+                tma_load_4d_pair(bs, tb, full_bar_leader, k0, nb, t.b, 0);
+            }
         }
     }
 
     __device__ static uint64_t a_desc(uint32_t addr, int pl, int ks) {
-        return GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>::template desc<A_MN, kTcBM>(addr, pl, ks);
+        return GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>::template desc<A_MN, kTcBM>(
+            addr + (ks / 4) * kASlabBytes, pl, ks % 4);
     }
     __device__ static uint64_t b_desc(uint32_t addr, int pl, int ks) {
-        return GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>::template desc<B_MN, kBH>(addr, pl, ks);
+        return GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>::template desc<B_MN, kBH>(
+            addr + (ks / 4) * kBSlabBytes, pl, ks % 4);
     }
 
     template <int COUNT>
