@@ -357,19 +357,21 @@ struct ConvEntry {
     int bn, planes;
     const void* fn;
     int smem, threads;
+    int kslabs;  // 32-channel slabs per K block
 };
 
-template <int BN, int PLANES>
+template <int BN, int PLANES, int KS = 1>
 ConvEntry make_conv_entry() {
-    using P = ConvProblem<BN, PLANES>;
+    using P = ConvProblem<BN, PLANES, KS>;
     using L = TcLayout<P>;
-    return ConvEntry{BN, PLANES, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes, L::kThreads};
+    return ConvEntry{BN, PLANES, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes, L::kThreads,
+                     KS};
 }
 
 const ConvEntry* conv_table(int* count) {
     static const ConvEntry table[] = {
-        make_conv_entry<16, 2>(), make_conv_entry<32, 2>(), make_conv_entry<64, 2>(), make_conv_entry<128, 2>(),
-        make_conv_entry<256, 2>(), make_conv_entry<16, 1>(), make_conv_entry<32, 1>(), make_conv_entry<64, 1>(),
+        make_conv_entry<16, 2>(), make_conv_entry<32, 2>(), make_conv_entry<64, 2, 2>(), make_conv_entry<128, 2>(),
+        make_conv_entry<256, 2>(), make_conv_entry<16, 1>(), make_conv_entry<32, 1>(), make_conv_entry<64, 1, 2>(),
         make_conv_entry<128, 1>(), make_conv_entry<256, 1>(),
     };
     *count = static_cast<int>(sizeof(table) / sizeof(table[0]));
@@ -391,17 +393,18 @@ const ConvEntry* pick_conv(int kf, int planes) {
     return best;
 }
 
-template <int BN, int PLANES>
+template <int BN, int PLANES, int KS = 1>
 ConvEntry make_wgrad_entry() {
-    using P = ConvWgradProblem<BN, PLANES>;
+    using P = ConvWgradProblem<BN, PLANES, KS>;
     using L = TcLayout<P>;
-    return ConvEntry{BN, PLANES, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes, L::kThreads};
+    return ConvEntry{BN, PLANES, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes, L::kThreads,
+                     KS};
 }
 
 const ConvEntry* wgrad_table(int* count) {
     static const ConvEntry table[] = {
-        make_wgrad_entry<64, 2>(), make_wgrad_entry<128, 2>(), make_wgrad_entry<256, 2>(),
-        make_wgrad_entry<64, 1>(), make_wgrad_entry<128, 1>(), make_wgrad_entry<256, 1>(),
+        make_wgrad_entry<64, 2, 2>(), make_wgrad_entry<128, 2>(), make_wgrad_entry<256, 2>(),
+        make_wgrad_entry<64, 1, 2>(), make_wgrad_entry<128, 1>(), make_wgrad_entry<256, 1>(),
     };
     *count = static_cast<int>(sizeof(table) / sizeof(table[0]));
     return table;
@@ -514,7 +517,7 @@ mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g,
     p.wp = wp;
     p.p_out = P;
     p.q_out = Q;
-    p.ncb = (cp + 31) / 32;
+    p.ncb = (cp + 32 * e->kslabs - 1) / (32 * e->kslabs);
     p.num_kb = r * s * p.ncb;
     p.tiles_pos = static_cast<int>((static_cast<long long>(P) * wp + kTcBM - 1) / kTcBM);
     p.tiles_f = (k + e->bn - 1) / e->bn;
@@ -612,7 +615,7 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     p.s = s;
     p.cg = cg;
     p.wp = wp;
-    p.kb_per_img = static_cast<int>((gpos + 31) / 32);
+    p.kb_per_img = static_cast<int>((gpos + 32 * e->kslabs - 1) / (32 * e->kslabs));
     p.rows_total = r * s * cg;
     p.tiles_m = (p.rows_total + kTcBM - 1) / kTcBM;
     p.tiles_f = (k + e->bn - 1) / e->bn;

@@ -34,20 +34,28 @@ struct ConvTcParams {
     unsigned long long wait_limit_ns;
 };
 
-template <int BN, int PLANES>
+template <int BN, int PLANES, int KS>
 constexpr int conv_stages() {
-    return (196608 / (PLANES * (kTcBM + BN) * 128)) > 8 ? 8 : (196608 / (PLANES * (kTcBM + BN) * 128));
+    return (196608 / (KS * PLANES * (kTcBM + BN) * 128)) > 8 ? 8
+                                                              : (196608 / (KS * PLANES * (kTcBM + BN) * 128));
 }
 
-template <int BN_, int PLANES_>
+// KS = 32-channel slabs per stage: a K block is (one tap, 32 * KS channels). Two slabs halve
+// the K blocks per tile and with them the fixed per-block cost of the MMA issuer (barrier wait,
+// fences, commit), which the narrow N <= 128 MMAs of a conv cannot hide.
+template <int BN_, int PLANES_, int KS_ = 1>
 struct ConvProblem {
     using Params = ConvTcParams;
     static constexpr int BN = BN_, PLANES = PLANES_, A_MN = 0, B_MN = 0;
+    static constexpr int KS = KS_;
     static constexpr bool kStackB = PLANES_ == 2 && BN_ <= 64;  // K-major weight tiles: hi, lo rows adjacent
-    static constexpr int STAGES = conv_stages<BN_, PLANES_>();
-    static constexpr int kATileBytes = PLANES * kTcBM * 128;
-    static constexpr int kBTileBytes = PLANES * BN * 128;
-    static constexpr int kKSteps = 4;  // 32 channels = 4 K steps of 8
+    static constexpr int STAGES = conv_stages<BN_, PLANES_, KS_>();
+    static constexpr int kASlabBytes = PLANES * kTcBM * 128;
+    static constexpr int kBSlabBytes = PLANES * BN * 128;
+    static constexpr int kATileBytes = KS * kASlabBytes;
+    static constexpr int kBTileBytes = KS * kBSlabBytes;
+    static constexpr int kKSteps = 4 * KS;  // 32 channels = 4 K steps of 8 per slab
+    static constexpr int kChunkKbOverride = 2 / KS;  // strict chunks stay 64 channels deep
     static_assert(STAGES >= 2, "conv tile configuration");
 
     struct Tile {
@@ -65,22 +73,29 @@ struct ConvProblem {
 
     __device__ static int valid_cols(const Params& p, const Tile& t) { return min(BN, p.kf - t.f0); }
 
+    // K block kb = (tap, group of KS 32-channel slabs); p.ncb counts such groups per tap.
+    // Slabs past the channels read the maps' zero fill.
     __device__ static void load(const Params& p, const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile,
                                 uint8_t* b_tile, uint64_t* bar, const Tile& t, int kb) {
         const int tap = kb / p.ncb;
-        const int c0 = (kb - tap * p.ncb) * 32;
         const int r = tap / p.s;
         const int sc = tap - r * p.s;
-        tma_load_4d(a_tile, ta, bar, c0, t.j0 + r * p.wp + sc, t.img, 0);
-        tma_load_4d(b_tile, tb, bar, c0, t.f0, tap, 0);
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            const int c0 = ((kb - tap * p.ncb) * KS + j) * 32;
+            tma_load_4d(a_tile + j * kASlabBytes, ta, bar, c0, t.j0 + r * p.wp + sc, t.img, 0);
+            tma_load_4d(b_tile + j * kBSlabBytes, tb, bar, c0, t.f0, tap, 0);
+        }
     }
 
-    // [plane][rows][32 channels], 128B swizzle: 8-row groups 1 KiB apart; a K step is 32 B.
+    // Per slab [plane][rows][32 channels], 128B swizzle: 8-row groups 1 KiB apart; a K step is 32 B.
     __device__ static uint64_t a_desc(uint32_t addr, int pl, int ks) {
-        return umma_smem_desc(addr + pl * kTcBM * 128 + ks * 32, 16, 1024, kLayoutSwizzle128B);
+        return umma_smem_desc(addr + (ks / 4) * kASlabBytes + pl * kTcBM * 128 + (ks % 4) * 32, 16, 1024,
+                              kLayoutSwizzle128B);
     }
     __device__ static uint64_t b_desc(uint32_t addr, int pl, int ks) {
-        return umma_smem_desc(addr + pl * BN * 128 + ks * 32, 16, 1024, kLayoutSwizzle128B);
+        return umma_smem_desc(addr + (ks / 4) * kBSlabBytes + pl * BN * 128 + (ks % 4) * 32, 16, 1024,
+                              kLayoutSwizzle128B);
     }
 
     // Scatters COUNT filters of one output position to NCHW: y = acc + bias[f].
@@ -126,15 +141,20 @@ struct ConvWgradParams {
     unsigned long long wait_limit_ns;
 };
 
-template <int BN_, int PLANES_>
+// KS = 32-position slabs per stage (a K block is 32 * KS positions; see ConvProblem).
+template <int BN_, int PLANES_, int KS_ = 1>
 struct ConvWgradProblem {
     using Params = ConvWgradParams;
     static constexpr int BN = BN_, PLANES = PLANES_, A_MN = 1, B_MN = 0;
+    static constexpr int KS = KS_;
     static constexpr bool kStackB = PLANES_ == 2 && BN_ <= 64;  // dY tiles are K-major: hi, lo rows adjacent
-    static constexpr int kATileBytes = PLANES * kTcBM * 128;
-    static constexpr int kBTileBytes = PLANES * BN * 128;
+    static constexpr int kASlabBytes = PLANES * kTcBM * 128;
+    static constexpr int kBSlabBytes = PLANES * BN * 128;
+    static constexpr int kATileBytes = KS * kASlabBytes;
+    static constexpr int kBTileBytes = KS * kBSlabBytes;
     static constexpr int STAGES = (196608 / (kATileBytes + kBTileBytes)) > 8 ? 8 : (196608 / (kATileBytes + kBTileBytes));
-    static constexpr int kKSteps = 4;
+    static constexpr int kKSteps = 4 * KS;
+    static constexpr int kChunkKbOverride = 2 / KS;  // strict chunks stay 64 positions deep
     static_assert(STAGES >= 2, "wgrad tile configuration");
 
     struct Tile {
@@ -152,30 +172,38 @@ struct ConvWgradProblem {
 
     __device__ static int valid_cols(const Params& p, const Tile& t) { return min(BN, p.kf - t.f0); }
 
+    // K block kb of the split: positions [j0, j0 + 32 * KS) of one image (p.kb_per_img blocks per image);
+    // slab j holds positions j0 + 32 j .. +31.
     __device__ static void load(const Params& p, const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile,
                                 uint8_t* b_tile, uint64_t* bar, const Tile& t, int kb) {
         const long long kg = static_cast<long long>(t.split) * p.kb_per_split + kb;
         const int img = static_cast<int>(kg / p.kb_per_img);
-        const int j0 = static_cast<int>(kg - static_cast<long long>(img) * p.kb_per_img) * 32;
+        const int j0 = static_cast<int>(kg - static_cast<long long>(img) * p.kb_per_img) * 32 * KS;
 #pragma unroll
-        for (int g = 0; g < kTcBM / 32; ++g) {
-            const int m = t.m0 + 32 * g;
-            const int tap = m / p.cg;
-            // rows past the last tap read channel coordinates beyond the map: zeros
-            const int c0 = tap < p.r * p.s ? m - tap * p.cg : p.cg;
-            const int rr = tap < p.r * p.s ? tap / p.s : 0;
-            const int shift = tap < p.r * p.s ? rr * p.wp + (tap - rr * p.s) : 0;
-            tma_load_4d(a_tile + g * PLANES * 4096, ta, bar, c0, j0 + shift, img, 0);
+        for (int j = 0; j < KS; ++j) {
+            const int js = j0 + 32 * j;
+#pragma unroll
+            for (int g = 0; g < kTcBM / 32; ++g) {
+                const int m = t.m0 + 32 * g;
+                const int tap = m / p.cg;
+                // rows past the last tap read channel coordinates beyond the map: zeros
+                const int c0 = tap < p.r * p.s ? m - tap * p.cg : p.cg;
+                const int rr = tap < p.r * p.s ? tap / p.s : 0;
+                const int shift = tap < p.r * p.s ? rr * p.wp + (tap - rr * p.s) : 0;
+                tma_load_4d(a_tile + j * kASlabBytes + g * PLANES * 4096, ta, bar, c0, js + shift, img, 0);
+            }
+            tma_load_4d(b_tile + j * kBSlabBytes, tb, bar, js, t.f0, img, 0);
         }
-        tma_load_4d(b_tile, tb, bar, j0, t.f0, img, 0);
     }
 
-    // A: [group of 32 M][plane][32 K rows][32 M] (128B swizzle, 32-byte atoms); B: [plane][BN][32 K].
+    // Per slab A: [group of 32 M][plane][32 K rows][32 M] (128B swizzle, 32-byte atoms); B: [plane][BN][32 K].
     __device__ static uint64_t a_desc(uint32_t addr, int pl, int ks) {
-        return umma_smem_desc(addr + pl * 4096 + ks * 1024, PLANES * 4096, 512, kLayoutSwizzle128B_Base32B);
+        return umma_smem_desc(addr + (ks / 4) * kASlabBytes + pl * 4096 + (ks % 4) * 1024, PLANES * 4096, 512,
+                              kLayoutSwizzle128B_Base32B);
     }
     __device__ static uint64_t b_desc(uint32_t addr, int pl, int ks) {
-        return umma_smem_desc(addr + pl * BN * 128 + ks * 32, 16, 1024, kLayoutSwizzle128B);
+        return umma_smem_desc(addr + (ks / 4) * kBSlabBytes + pl * BN * 128 + (ks % 4) * 32, 16, 1024,
+                              kLayoutSwizzle128B);
     }
 
     template <int COUNT>

@@ -30,6 +30,7 @@
 #include "mfb_device.cuh"
 
 #include <cuda.h>
+#include <type_traits>
 
 namespace mfb {
 
@@ -60,6 +61,13 @@ template <class Prob>
 constexpr int tc_acc_cols() {
     return Prob::kStackB ? 2 * Prob::BN : Prob::BN;
 }
+
+// K blocks per strict accumulator chunk: kChunkKb, or Prob::kChunkKbOverride for policies
+// whose K blocks are deeper than 32 (the chunk stays 64 deep).
+template <class P, class = void>
+struct TcChunk : std::integral_constant<int, kChunkKb> {};
+template <class P>
+struct TcChunk<P, std::void_t<decltype(P::kChunkKbOverride)>> : std::integral_constant<int, P::kChunkKbOverride> {};
 
 template <class Prob>
 struct TcLayout {
@@ -119,7 +127,7 @@ __device__ __forceinline__ void tc_epilogue_role(const typename Prob::Params& p,
             float sum[kCols];
 #pragma unroll
             for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
-            const int n_chunks = (num_kb + kChunkKb - 1) / kChunkKb;
+            const int n_chunks = (num_kb + TcChunk<Prob>::value - 1) / TcChunk<Prob>::value;
             for (int c = 0; c < n_chunks; ++c, ++buf) {
                 const int b = buf & 1;
                 if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
@@ -279,7 +287,7 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
         constexpr uint32_t idesc = umma_idesc_tf32(kTcBM, BN, Prob::A_MN, Prob::B_MN);
         constexpr uint32_t idesc_stacked = umma_idesc_tf32(kTcBM, 2 * BN, Prob::A_MN, Prob::B_MN);
         // Accumulator buffers are handed out per tile (tf32) or per K chunk (strict).
-        const int kb_per_buf = PLANES == 2 ? kChunkKb : 0x7fffffff;
+        const int kb_per_buf = PLANES == 2 ? TcChunk<Prob>::value : 0x7fffffff;
         int it = 0;   // K blocks consumed (stage ring position)
         int buf = 0;  // accumulator buffers used so far
         bool ok = true;
