@@ -201,12 +201,12 @@ struct TcEntry {
     int kslabs;  // 32-deep K slabs per stage (the kernel's K block is 32 * kslabs deep)
 };
 
-template <int BN, int STAGES, int PLANES, int A_MN, int B_MN>
+template <int BN, int STAGES, int PLANES, int A_MN, int B_MN, int KS = 1>
 TcEntry make_entry() {
-    using P = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>;
+    using P = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN, KS>;
     using L = TcLayout<P>;
     return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes,
-                   L::kThreads, 0, 1};
+                   L::kThreads, 0, KS};
 }
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN, int KS = 1>
@@ -231,17 +231,17 @@ const TcEntry* kernel_table(int* count) {
         // strict FP32 (3xTF32 split planes, chunked round-to-nearest accumulation)
         make_entry<256, 2, 2, 0, 1>(),
         make_entry<128, 3, 2, 0, 1>(),
-        make_entry<64, 4, 2, 0, 1>(),
+        make_entry<64, 2, 2, 0, 1, 2>(),
         make_entry<128, 3, 2, 1, 1>(),
         make_entry<128, 3, 2, 0, 0>(),
         make_entry<128, 3, 2, 1, 0>(),
         // TF32 single pass
-        make_entry<256, 4, 1, 0, 1>(),
-        make_entry<128, 6, 1, 0, 1>(),
-        make_entry<64, 8, 1, 0, 1>(),
-        make_entry<128, 6, 1, 1, 1>(),
-        make_entry<128, 6, 1, 0, 0>(),
-        make_entry<128, 6, 1, 1, 0>(),
+        make_entry<256, 2, 1, 0, 1, 2>(),
+        make_entry<128, 3, 1, 0, 1, 2>(),
+        make_entry<64, 4, 1, 0, 1, 2>(),
+        make_entry<128, 3, 1, 1, 1, 2>(),
+        make_entry<128, 3, 1, 0, 0, 2>(),
+        make_entry<128, 3, 1, 1, 0, 2>(),
     };
     *count = static_cast<int>(sizeof(table) / sizeof(table[0]));
     return table;

@@ -33,14 +33,21 @@ struct GemmTcParams {
 
 constexpr int kBK = 32;  // 32 fp32 = 128 bytes of K per stage: one swizzle row
 
-template <int BN_, int STAGES_, int PLANES_, int A_MN_, int B_MN_>
+// KS = 32-deep K slabs per stage: a K block is 32 * KS deep. Two slabs halve the fixed cost
+// the MMA issuer pays per K block (barrier wait, fences, commit), which matters when a block
+// holds few MMAs (TF32, narrow tiles). Strict accumulator chunks stay 64 deep.
+template <int BN_, int STAGES_, int PLANES_, int A_MN_, int B_MN_, int KS_ = 1>
 struct GemmProblem {
     using Params = GemmTcParams;
     static constexpr int BN = BN_, STAGES = STAGES_, PLANES = PLANES_, A_MN = A_MN_, B_MN = B_MN_;
+    static constexpr int KS = KS_;
     static constexpr bool kStackB = false;  // row-major B is MN-major: its planes interleave per 32 columns
-    static constexpr int kATileBytes = PLANES * kTcBM * kBK * 4;
-    static constexpr int kBTileBytes = PLANES * BN * kBK * 4;
-    static constexpr int kKSteps = kBK / 8;
+    static constexpr int kASlabBytes = PLANES * kTcBM * kBK * 4;
+    static constexpr int kBSlabBytes = PLANES * BN * kBK * 4;
+    static constexpr int kATileBytes = KS * kASlabBytes;
+    static constexpr int kBTileBytes = KS * kBSlabBytes;
+    static constexpr int kKSteps = KS * kBK / 8;
+    static constexpr int kChunkKbOverride = KS == 1 ? kChunkKb : 1;
 
     struct Tile {
         int m0, n0, b;
@@ -65,20 +72,25 @@ struct GemmProblem {
 
     __device__ static void load(const Params&, const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile,
                                 uint8_t* b_tile, uint64_t* bar, const Tile& t, int kb) {
-        const int k0 = kb * kBK;
-        if (A_MN) {
 #pragma unroll
-            for (int g = 0; g < kTcBM / 32; ++g)
-                tma_load_4d(a_tile + g * PLANES * 4096, ta, bar, t.m0 + 32 * g, k0, t.b, 0);
-        } else {
-            tma_load_4d(a_tile, ta, bar, k0, t.m0, t.b, 0);
-        }
-        if (B_MN) {
+        for (int j = 0; j < KS; ++j) {
+            const int k0 = (kb * KS + j) * kBK;
+            uint8_t* as = a_tile + j * kASlabBytes;
+            uint8_t* bs = b_tile + j * kBSlabBytes;
+            if (A_MN) {
 #pragma unroll
-            for (int g = 0; g < BN / 32; ++g)
-                tma_load_4d(b_tile + g * PLANES * 4096, tb, bar, t.n0 + 32 * g, k0, t.b, 0);
-        } else {
-            tma_load_4d(b_tile, tb, bar, k0, t.n0, t.b, 0);
+                for (int g = 0; g < kTcBM / 32; ++g)
+                    tma_load_4d(as + g * PLANES * 4096, ta, bar, t.m0 + 32 * g, k0, t.b, 0);
+            } else {
+                tma_load_4d(as, ta, bar, k0, t.m0, t.b, 0);
+            }
+            if (B_MN) {
+#pragma unroll
+                for (int g = 0; g < BN / 32; ++g)
+                    tma_load_4d(bs + g * PLANES * 4096, tb, bar, t.n0 + 32 * g, k0, t.b, 0);
+            } else {
+                tma_load_4d(bs, tb, bar, k0, t.n0, t.b, 0);
+            }
         }
     }
 
@@ -93,8 +105,12 @@ struct GemmProblem {
         // [plane][ROWS][32 K]: 8-row groups 1 KiB apart (SBO); a K step of 8 is 32 B.
         return umma_smem_desc(addr + pl * ROWS * 128 + ks * 32, 16, 1024, kLayoutSwizzle128B);
     }
-    __device__ static uint64_t a_desc(uint32_t addr, int pl, int ks) { return desc<A_MN, kTcBM>(addr, pl, ks); }
-    __device__ static uint64_t b_desc(uint32_t addr, int pl, int ks) { return desc<B_MN, BN>(addr, pl, ks); }
+    __device__ static uint64_t a_desc(uint32_t addr, int pl, int ks) {
+        return desc<A_MN, kTcBM>(addr + (ks / 4) * kASlabBytes, pl, ks % 4);
+    }
+    __device__ static uint64_t b_desc(uint32_t addr, int pl, int ks) {
+        return desc<B_MN, BN>(addr + (ks / 4) * kBSlabBytes, pl, ks % 4);
+    }
 
     // Writes COUNT consecutive outputs of one row: o = epilogue(alpha * acc + beta * C).
     template <int COUNT>

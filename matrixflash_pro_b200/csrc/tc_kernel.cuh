@@ -75,6 +75,8 @@ struct TcLayout {
     static constexpr int kBarrierOffset = Prob::STAGES * kStageBytes;
     static constexpr int kBytes = kBarrierOffset + 256 + 1024;  // barriers + 1 KiB alignment slack
     static constexpr int kTmemCols = 2 * tc_acc_cols<Prob>() < 32 ? 32 : 2 * tc_acc_cols<Prob>();
+    // tcgen05.alloc takes a power of two of at most 512 columns
+    static_assert(kTmemCols <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation");
     static constexpr int kEpiWarps = Prob::PLANES == 2 ? 8 : 4;
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };

@@ -28,14 +28,14 @@
 
 namespace mfb {
 
-// KS = 32-deep K slabs per stage (a K block is 32 * KS deep; KS = 2 only for TF32, whose
-// accumulator is not chunked).
+// KS = 32-deep K slabs per stage (a K block is 32 * KS deep; strict accumulator chunks stay
+// 64 deep whatever KS is).
 template <int BN_, int STAGES_, int PLANES_, int A_MN_, int B_MN_, int KS_ = 1>
 struct GemmPairProblem {
     using Params = GemmTcParams;
     static constexpr int BN = BN_, STAGES = STAGES_, PLANES = PLANES_, A_MN = A_MN_, B_MN = B_MN_;
     static constexpr int KS = KS_;
-    static_assert(KS == 1 || PLANES == 1, "strict chunking counts 32-deep K blocks");
+    static constexpr int kChunkKbOverride = KS == 1 ? kChunkKb : 1;  // strict chunks stay 64 deep
     static constexpr int kBH = BN / 2;  // B columns per CTA
     static constexpr int kASlabBytes = PLANES * kTcBM * kBK * 4;
     static constexpr int kBSlabBytes = PLANES * kBH * kBK * 4;
@@ -114,7 +114,10 @@ struct TcPairLayout {
     static constexpr int kStageBytes = Prob::kATileBytes + Prob::kBTileBytes;
     static constexpr int kBarrierOffset = Prob::STAGES * kStageBytes;
     static constexpr int kBytes = kBarrierOffset + 256 + 1024;
-    static constexpr int kTmemCols = 2 * Prob::BN;
+    // tcgen05.alloc takes a power of two >= 32 columns: two BN-wide accumulator buffers, rounded up.
+    static constexpr int kTmemCols = 2 * Prob::BN <= 32 ? 32 : 2 * Prob::BN <= 64 ? 64 : 2 * Prob::BN <= 128 ? 128
+                                     : 2 * Prob::BN <= 256 ? 256 : 512;
+    static_assert(2 * Prob::BN <= 512 && (kTmemCols & (kTmemCols - 1)) == 0, "TMEM allocation");
     static constexpr int kEpiWarps = Prob::PLANES == 2 ? 8 : 4;
     static constexpr int kThreads = 64 + 32 * kEpiWarps;
 };
@@ -211,7 +214,7 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
     } else if (warp == 1 && lane == 0 && leader) {
         // ------------------------------------------------------------ MMA issuer (leader)
         constexpr uint32_t idesc = umma_idesc_tf32(2 * kTcBM, BN, Prob::A_MN, Prob::B_MN);
-        const int kb_per_buf = PLANES == 2 ? kChunkKb : 0x7fffffff;
+        const int kb_per_buf = PLANES == 2 ? TcChunk<Prob>::value : 0x7fffffff;
         int it = 0;
         int buf = 0;
         bool ok = true;
@@ -276,7 +279,7 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
                 float sum[kCols];
 #pragma unroll
                 for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
-                const int n_chunks = (num_kb + kChunkKb - 1) / kChunkKb;
+                const int n_chunks = (num_kb + TcChunk<Prob>::value - 1) / TcChunk<Prob>::value;
                 for (int c = 0; c < n_chunks; ++c, ++buf) {
                     const int b = buf & 1;
                     if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
