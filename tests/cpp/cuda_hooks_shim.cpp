@@ -1,4 +1,4 @@
-// The reference-side binding of INTEGRATION.md §1, compiled as a stand-alone program:
+// The reference-side binding of hw::cuda_gemm, compiled as a stand-alone program:
 // matrix_pro::hw::cuda_gemm / cuda_sync (include/matrix_pro/detail/cuda_hooks.hpp:17-18,28)
 // implemented over libmfb.so's C ABI, then exercised the way CudaDriver::gemm
 // (src/hw/cuda_backend.cu:274-277) uses them. Exit code 0 = all checks passed.

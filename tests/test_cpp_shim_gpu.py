@@ -1,4 +1,4 @@
-"""GPU tier: the C++ drop-in of INTEGRATION.md §1 (matrix_pro::hw::cuda_gemm over the C ABI),
+"""GPU tier: the C++ drop-in body of matrix_pro::hw::cuda_gemm / cuda_sync over the C ABI,
 compiled with g++ against include/mfb.h and libmfb.so and run as its own process."""
 import os
 import subprocess
