@@ -370,33 +370,27 @@ ConvEntry make_conv_entry() {
 
 const ConvEntry* conv_table(int* count) {
     static const ConvEntry table[] = {
-        // narrow tiles with one or two 32-channel slabs per K block, wide tiles with one
-        make_conv_entry<16, 2>(), make_conv_entry<16, 2, 2>(), make_conv_entry<32, 2>(), make_conv_entry<32, 2, 2>(),
-        make_conv_entry<64, 2>(), make_conv_entry<64, 2, 2>(), make_conv_entry<128, 2>(), make_conv_entry<256, 2>(),
-        make_conv_entry<16, 1>(), make_conv_entry<16, 1, 2>(), make_conv_entry<32, 1>(), make_conv_entry<32, 1, 2>(),
-        make_conv_entry<64, 1>(), make_conv_entry<64, 1, 2>(), make_conv_entry<128, 1>(), make_conv_entry<256, 1>(),
+        // narrow tiles: 2 (strict) or 4 (TF32) 32-channel slabs per K block; wide tiles: 1
+        make_conv_entry<16, 2, 2>(), make_conv_entry<32, 2, 2>(), make_conv_entry<64, 2, 2>(), make_conv_entry<128, 2>(),
+        make_conv_entry<256, 2>(), make_conv_entry<16, 1, 4>(), make_conv_entry<32, 1, 4>(), make_conv_entry<64, 1, 4>(),
+        make_conv_entry<128, 1>(), make_conv_entry<256, 1>(),
     };
     *count = static_cast<int>(sizeof(table) / sizeof(table[0]));
     return table;
 }
 
 // Narrowest filter tile that covers K (one filter tile per position tile when K <= 256).
-// Two 32-channel slabs per K block where the channels fill whole pairs of slabs (an odd
-// slab count would load and multiply a slab of zero fill in every block): measured on
-// 64 x 64 x 56 x 56 with 24 filters +19% strict / +25% TF32, and with C = 32 -20% if forced.
-const ConvEntry* pick_conv(int kf, int planes, int cp) {
+const ConvEntry* pick_conv(int kf, int planes) {
     int count = 0;
     const ConvEntry* t = conv_table(&count);
-    const int want_ks = ((cp + 31) / 32) % 2 == 0 ? 2 : 1;
-    int bn = 0;
-    for (int i = 0; i < count; ++i)
-        if (t[i].planes == planes && t[i].bn >= kf && (bn == 0 || t[i].bn < bn)) bn = t[i].bn;
-    if (bn == 0)
-        for (int i = 0; i < count; ++i)
-            if (t[i].planes == planes && t[i].bn > bn) bn = t[i].bn;
     const ConvEntry* best = nullptr;
-    for (int i = 0; i < count; ++i)
-        if (t[i].planes == planes && t[i].bn == bn && (!best || t[i].kslabs == want_ks)) best = &t[i];
+    for (int i = 0; i < count; ++i) {
+        if (t[i].planes != planes) continue;
+        if (t[i].bn >= kf && (!best || t[i].bn < best->bn)) best = &t[i];
+    }
+    if (!best)
+        for (int i = 0; i < count; ++i)
+            if (t[i].planes == planes && (!best || t[i].bn > best->bn)) best = &t[i];
     return best;
 }
 
@@ -459,7 +453,7 @@ mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g,
     const int hp = h + 2 * g.pad_h, wp = w + 2 * g.pad_w;
     const long long npos = static_cast<long long>(hp) * wp;
     if (n > 65535 || npos > 0x7fffffffLL) return fail(MFB_EUNSUPPORTED, "conv2d input too large");
-    const ConvEntry* e = pick_conv(k, planes, cp);
+    const ConvEntry* e = pick_conv(k, planes);
     if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 conv configuration");
 
     const size_t need = conv_tc_workspace_bytes(g, precision);
@@ -524,8 +518,8 @@ mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g,
     p.wp = wp;
     p.p_out = P;
     p.q_out = Q;
-    p.ncb = (cp + 32 * e->kslabs - 1) / (32 * e->kslabs);
-    p.num_kb = r * s * p.ncb;
+    p.ncb = (cp + 31) / 32;  // 32-channel slabs per tap
+    p.num_kb = (r * s * p.ncb + e->kslabs - 1) / e->kslabs;
     p.tiles_pos = static_cast<int>((static_cast<long long>(P) * wp + kTcBM - 1) / kTcBM);
     p.tiles_f = (k + e->bn - 1) / e->bn;
     p.y = y;

@@ -25,7 +25,7 @@ struct ConvTcParams {
     int n_img, c, h, w, kf, r, s, pad;
     int hp, wp;         // padded input height / width
     int p_out, q_out;   // output height / width
-    int ncb;            // 32-channel K blocks per tap
+    int ncb;            // 32-channel slabs per tap (K blocks span KS consecutive slabs)
     int num_kb;         // r * s * ncb
     int tiles_pos;      // ceil(p_out * wp / 128) position tiles per image
     int tiles_f;        // filter tiles
@@ -55,7 +55,8 @@ struct ConvProblem {
     static constexpr int kATileBytes = KS * kASlabBytes;
     static constexpr int kBTileBytes = KS * kBSlabBytes;
     static constexpr int kKSteps = 4 * KS;  // 32 channels = 4 K steps of 8 per slab
-    static constexpr int kChunkKbOverride = 2 / KS;  // strict chunks stay 64 channels deep
+    static_assert(KS == 1 || KS == 2 || (KS == 4 && PLANES_ == 1), "slabs per K block");
+    static constexpr int kChunkKbOverride = KS == 1 ? 2 : 1;  // strict chunks stay 64 channels deep
     static_assert(STAGES >= 2, "conv tile configuration");
 
     struct Tile {
@@ -73,16 +74,24 @@ struct ConvProblem {
 
     __device__ static int valid_cols(const Params& p, const Tile& t) { return min(BN, p.kf - t.f0); }
 
-    // K block kb = (tap, group of KS 32-channel slabs); p.ncb counts such groups per tap.
-    // Slabs past the channels read the maps' zero fill.
+    // The tile's K runs over (tap, 32-channel slab) pairs, tap-major, p.ncb slabs per tap; K block
+    // kb holds slabs kb*KS .. kb*KS+KS-1, so a block may span two taps and no slab is wasted when
+    // the channel count fills an odd number of slabs. Channels past Cp and the slabs after the
+    // last tap (the tail of the last block) read the maps' zero fill.
     __device__ static void load(const Params& p, const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile,
                                 uint8_t* b_tile, uint64_t* bar, const Tile& t, int kb) {
-        const int tap = kb / p.ncb;
-        const int r = tap / p.s;
-        const int sc = tap - r * p.s;
+        const int taps = p.r * p.s;
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
-            const int c0 = ((kb - tap * p.ncb) * KS + j) * 32;
+            const int g = kb * KS + j;
+            int tap = g / p.ncb;
+            int c0 = (g - tap * p.ncb) * 32;
+            if (tap >= taps) {  // past the last tap: a box beyond the channels, all zero fill
+                tap = taps - 1;
+                c0 = p.ncb * 32;
+            }
+            const int r = tap / p.s;
+            const int sc = tap - r * p.s;
             tma_load_4d(a_tile + j * kASlabBytes, ta, bar, c0, t.j0 + r * p.wp + sc, t.img, 0);
             tma_load_4d(b_tile + j * kBSlabBytes, tb, bar, c0, t.f0, tap, 0);
         }
