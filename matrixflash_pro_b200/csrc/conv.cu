@@ -520,6 +520,8 @@ mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g,
     p.q_out = Q;
     p.ncb = (cp + 31) / 32;  // 32-channel slabs per tap
     p.num_kb = (r * s * p.ncb + e->kslabs - 1) / e->kslabs;
+    p.div_ncb = make_fastdiv(static_cast<uint32_t>(p.ncb));
+    p.div_s = make_fastdiv(static_cast<uint32_t>(s));
     p.tiles_pos = static_cast<int>((static_cast<long long>(P) * wp + kTcBM - 1) / kTcBM);
     p.tiles_f = (k + e->bn - 1) / e->bn;
     p.y = y;
@@ -597,8 +599,10 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     const long long npos = static_cast<long long>(hp) * wp;
     const long long gpos = static_cast<long long>(P) * wp;
     const ConvEntry* e = pick_wgrad(k, planes);
+    // The producer indexes K blocks within a split as 32-bit values: n * P * Wp / 32 < 2^30 keeps
+    // them below 2^31 (the planes of any problem that fits in device memory are far smaller).
     const bool tensor = stride == 1 && flops >= kConvDirectMaxFlops && e != nullptr && n <= 65535 &&
-                        npos <= 0x7fffffffLL && gpos <= 0x7fffffffLL;
+                        npos <= 0x7fffffffLL && gpos <= 0x7fffffffLL && n * ((gpos + 31) / 32) < (1LL << 30);
     if (!tensor) {
         const int blocks = static_cast<int>(std::min<long long>((wtotal + 127) / 128, 148LL * 16));
         conv_bwd_filter_direct_kernel<<<blocks, 128, 0, stream>>>(dy, x, dw, n, c, h, w, k, r, s, P, Q, stride, pad);
@@ -617,6 +621,7 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     p.cg = cg;
     p.wp = wp;
     p.kb_per_img = static_cast<int>((gpos + 32 * e->kslabs - 1) / (32 * e->kslabs));
+    p.div_kb_per_img = make_fastdiv(static_cast<uint32_t>(p.kb_per_img));
     p.rows_total = r * s * cg;
     p.tiles_m = (p.rows_total + kTcBM - 1) / kTcBM;
     p.tiles_f = (k + e->bn - 1) / e->bn;

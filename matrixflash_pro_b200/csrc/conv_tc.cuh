@@ -17,6 +17,7 @@
 // multiple of 32. Channels beyond Cp and positions beyond the image read as zeros.
 #pragma once
 
+#include "fastdiv.h"
 #include "tc_kernel.cuh"
 
 namespace mfb {
@@ -26,6 +27,8 @@ struct ConvTcParams {
     int hp, wp;         // padded input height / width
     int p_out, q_out;   // output height / width
     int ncb;            // 32-channel slabs per tap (K blocks span KS consecutive slabs)
+    FastDiv div_ncb;    // division by ncb
+    FastDiv div_s;      // division by s
     int num_kb;         // r * s * ncb
     int tiles_pos;      // ceil(p_out * wp / 128) position tiles per image
     int tiles_f;        // filter tiles
@@ -84,13 +87,13 @@ struct ConvProblem {
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
             const int g = kb * KS + j;
-            int tap = g / p.ncb;
+            int tap = static_cast<int>(fastdiv(static_cast<uint32_t>(g), p.div_ncb));
             int c0 = (g - tap * p.ncb) * 32;
             if (tap >= taps) {  // past the last tap: a box beyond the channels, all zero fill
                 tap = taps - 1;
                 c0 = p.ncb * 32;
             }
-            const int r = tap / p.s;
+            const int r = static_cast<int>(fastdiv(static_cast<uint32_t>(tap), p.div_s));
             const int sc = tap - r * p.s;
             tma_load_4d(a_tile + j * kASlabBytes, ta, bar, c0, t.j0 + r * p.wp + sc, t.img, 0);
             tma_load_4d(b_tile + j * kBSlabBytes, tb, bar, c0, t.f0, tap, 0);
@@ -140,7 +143,8 @@ struct ConvWgradParams {
     int n_img, c, kf, r, s;
     int cg;              // C rounded up to 32
     int wp;              // padded width of X (output positions live in this width)
-    int kb_per_img;      // ceil(P * Wp / 32)
+    int kb_per_img;      // ceil(P * Wp / (32 * KS))
+    FastDiv div_kb_per_img;
     int kb_per_split;
     int splits;
     int tiles_m, tiles_f;
@@ -166,8 +170,13 @@ struct ConvWgradProblem {
     static constexpr int kChunkKbOverride = 2 / KS;  // strict chunks stay 64 positions deep
     static_assert(STAGES >= 2, "wgrad tile configuration");
 
+    // The box coordinates of the tile's four 32-row groups (channel, position shift of the
+    // tap) and where its K range starts (image, K block within the image) are fixed per
+    // tile; the producer derives them once here instead of per K block.
     struct Tile {
         int m0, f0, split;
+        int img0, kb0;  // first K block of the split: image, block within the image
+        int c0[kTcBM / 32], shift[kTcBM / 32];
     };
 
     __device__ static int num_tiles(const Params& p) { return p.tiles_m * p.tiles_f * p.splits; }
@@ -176,31 +185,42 @@ struct ConvWgradProblem {
     __device__ static Tile tile(const Params& p, int t) {
         const int split = t / (p.tiles_m * p.tiles_f);
         const int rest = t - split * p.tiles_m * p.tiles_f;
-        return Tile{(rest / p.tiles_f) * kTcBM, (rest % p.tiles_f) * BN, split};
+        Tile out;
+        out.m0 = (rest / p.tiles_f) * kTcBM;
+        out.f0 = (rest % p.tiles_f) * BN;
+        out.split = split;
+        const long long kg = static_cast<long long>(split) * p.kb_per_split;
+        out.img0 = static_cast<int>(kg / p.kb_per_img);
+        out.kb0 = static_cast<int>(kg - static_cast<long long>(out.img0) * p.kb_per_img);
+#pragma unroll
+        for (int g = 0; g < kTcBM / 32; ++g) {
+            const int m = out.m0 + 32 * g;
+            const int tap = m / p.cg;
+            // rows past the last tap read channel coordinates beyond the map: zeros
+            const bool real = tap < p.r * p.s;
+            const int rr = real ? tap / p.s : 0;
+            out.c0[g] = real ? m - tap * p.cg : p.cg;
+            out.shift[g] = real ? rr * p.wp + (tap - rr * p.s) : 0;
+        }
+        return out;
     }
 
     __device__ static int valid_cols(const Params& p, const Tile& t) { return min(BN, p.kf - t.f0); }
 
     // K block kb of the split: positions [j0, j0 + 32 * KS) of one image (p.kb_per_img blocks per image);
-    // slab j holds positions j0 + 32 j .. +31.
+    // slab j holds positions j0 + 32 j .. +31. t.kb0 + kb stays below 2^31 (checked on the host).
     __device__ static void load(const Params& p, const CUtensorMap* ta, const CUtensorMap* tb, uint8_t* a_tile,
                                 uint8_t* b_tile, uint64_t* bar, const Tile& t, int kb) {
-        const long long kg = static_cast<long long>(t.split) * p.kb_per_split + kb;
-        const int img = static_cast<int>(kg / p.kb_per_img);
-        const int j0 = static_cast<int>(kg - static_cast<long long>(img) * p.kb_per_img) * 32 * KS;
+        const int rel = t.kb0 + kb;
+        const int q = static_cast<int>(fastdiv(static_cast<uint32_t>(rel), p.div_kb_per_img));
+        const int img = t.img0 + q;
+        const int j0 = (rel - q * p.kb_per_img) * 32 * KS;
 #pragma unroll
         for (int j = 0; j < KS; ++j) {
             const int js = j0 + 32 * j;
 #pragma unroll
-            for (int g = 0; g < kTcBM / 32; ++g) {
-                const int m = t.m0 + 32 * g;
-                const int tap = m / p.cg;
-                // rows past the last tap read channel coordinates beyond the map: zeros
-                const int c0 = tap < p.r * p.s ? m - tap * p.cg : p.cg;
-                const int rr = tap < p.r * p.s ? tap / p.s : 0;
-                const int shift = tap < p.r * p.s ? rr * p.wp + (tap - rr * p.s) : 0;
-                tma_load_4d(a_tile + j * kASlabBytes + g * PLANES * 4096, ta, bar, c0, js + shift, img, 0);
-            }
+            for (int g = 0; g < kTcBM / 32; ++g)
+                tma_load_4d(a_tile + j * kASlabBytes + g * PLANES * 4096, ta, bar, t.c0[g], js + t.shift[g], img, 0);
             tma_load_4d(b_tile + j * kBSlabBytes, tb, bar, js, t.f0, img, 0);
         }
     }
