@@ -52,6 +52,7 @@ SHAPES = [
     (3, 16, 21, 19, 24, 5, 5, 1, 2),     # 5x5, pad 2
     (2, 32, 20, 20, 48, 3, 3, 1, 0),     # pad 0: input-gradient padding R - 1 = 2
     (64, 32, 12, 12, 64, 1, 1, 1, 0),    # 1x1
+    (52, 48, 24, 24, 40, 3, 3, 1, 1),    # 48 channels: the input gradient's conv has 48 "filters"
     (2, 6, 11, 9, 5, 3, 3, 2, 1),        # stride 2: direct kernels
     (1, 3, 8, 8, 4, 3, 3, 1, 1),         # tiny: direct kernels
 ]
