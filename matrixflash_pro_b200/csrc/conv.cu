@@ -263,19 +263,32 @@ __global__ void conv_pack_grad_kernel(const float* __restrict__ dy, int kf, int 
 }
 
 // dW[f][c][r][s] = sum over splits, in split order, of the partial tiles of the weight-gradient GEMM.
+// Threads walk the partial rows (m = tap * cg + channel) with the filter index fastest, so a warp
+// reads 128 contiguous bytes per split; the loads of 16 splits are issued before their adds,
+// which stay in split order.
 __global__ void conv_wgrad_reduce_kernel(const float* __restrict__ partial, int splits, long long rows_alloc,
                                          int ld_partial, int kf, int c, int taps, int cg, float* __restrict__ dw) {
-    const long long total = static_cast<long long>(kf) * c * taps;
+    const long long total = static_cast<long long>(taps) * cg * kf;
     for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int tap = static_cast<int>(idx % taps);
-        const long long rest = idx / taps;
-        const int ch = static_cast<int>(rest % c);
-        const int f = static_cast<int>(rest / c);
-        const long long m = static_cast<long long>(tap) * cg + ch;
+        const int f = static_cast<int>(idx % kf);
+        const long long m = idx / kf;
+        const int tap = static_cast<int>(m / cg);
+        const int ch = static_cast<int>(m - static_cast<long long>(tap) * cg);
+        if (ch >= c) continue;
+        const float* src = partial + m * ld_partial + f;
+        const long long step = rows_alloc * ld_partial;
         float sum = 0.0f;
-        for (int sp = 0; sp < splits; ++sp) sum += partial[(sp * rows_alloc + m) * ld_partial + f];
-        dw[idx] = sum;
+        int sp = 0;
+        for (; sp + 16 <= splits; sp += 16) {
+            float v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = src[(sp + u) * step];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) sum += v[u];
+        }
+        for (; sp < splits; ++sp) sum += src[sp * step];
+        dw[(static_cast<long long>(f) * c + ch) * taps + tap] = sum;
     }
 }
 
@@ -337,12 +350,22 @@ __global__ void conv_bwd_filter_direct_kernel(const float* __restrict__ grad, co
     }
 }
 
-// dB[f] = sum over images, in image order, of the per-(image, filter) row sums.
+// dB[f] = sum over images, in image order, of the per-(image, filter) row sums. The loads of
+// 16 images are issued before their adds, which stay in image order (one dependent load per
+// image made the kernel L2-latency-bound).
 __global__ void conv_bias_images_kernel(const float* __restrict__ row_sums, int n, int kf, float* __restrict__ db) {
     const int f = blockIdx.x * blockDim.x + threadIdx.x;
     if (f >= kf) return;
     float acc = 0.0f;
-    for (int img = 0; img < n; ++img) acc += row_sums[static_cast<long long>(img) * kf + f];
+    int img = 0;
+    for (; img + 16 <= n; img += 16) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = row_sums[static_cast<long long>(img + u) * kf + f];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc += v[u];
+    }
+    for (; img < n; ++img) acc += row_sums[static_cast<long long>(img) * kf + f];
     db[f] = acc;
 }
 
