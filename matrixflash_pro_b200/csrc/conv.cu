@@ -243,20 +243,29 @@ mfb_status_t conv2d_direct(cudaStream_t stream, int n, int c, int h, int w, int 
 // ------------------------------------------------------------------------------------ backward kernels
 
 // dy (N,K,P,Q) -> G [N][K][ldy]: output positions j = p*Wp + q of X's padded width, zeros for
-// q >= Q and j >= P*Wp; 4 positions per thread.
-__global__ void conv_pack_grad_kernel(const float* __restrict__ dy, int kf, int P, int Q, int wp, int ldy,
-                                      long long groups, float* __restrict__ hi, float* __restrict__ lo) {
-    const int per_row = ldy / 4;
-    for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < groups;
-         idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const long long row = idx / per_row;  // img * kf + f
-        const int j0 = static_cast<int>(idx - row * per_row) * 4;
+// q >= Q and j >= P*Wp. grid (ceil(ldy / 4 / 128), up to 16 x 148 row slots): a thread writes 4
+// positions of every grid.y-th (image, filter) row; one multiply-shift division locates its first
+// position, the others follow by wrapping q (no per-element integer division: the kernel was
+// issue-bound).
+__global__ void __launch_bounds__(128) conv_pack_grad_kernel(const float* __restrict__ dy, int P, int Q, int wp,
+                                                             int ldy, long long rows, FastDiv div_wp,
+                                                             float* __restrict__ hi, float* __restrict__ lo) {
+    const int j0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (j0 >= ldy) return;
+    const int pr0 = static_cast<int>(fastdiv(static_cast<uint32_t>(j0), div_wp));
+    const int q0 = j0 - pr0 * wp;
+#pragma unroll 4
+    for (long long row = blockIdx.y; row < rows; row += gridDim.y) {
+        const float* src = dy + row * P * Q;
+        int pr = pr0, q = q0;
         float v[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const int j = j0 + e;
-            const int pr = j / wp, q = j - (j / wp) * wp;
-            v[e] = (pr < P && q < Q) ? __ldg(dy + (row * P + pr) * Q + q) : 0.0f;
+            v[e] = (pr < P && q < Q) ? __ldg(src + static_cast<long long>(pr) * Q + q) : 0.0f;
+            if (++q == wp) {
+                q = 0;
+                ++pr;
+            }
         }
         write_planes4(hi, lo, row * ldy + j0, v[0], v[1], v[2], v[3]);
     }
@@ -691,9 +700,10 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
         conv_pack_input_kernel<<<pgrid, 256, 0, stream>>>(x, c, h, w, pad, pad, cp, hp, wp, a_hi, a_lo);
     }
     MFB_CUDA_TRY(cudaGetLastError(), "wgrad input prepass launch");
-    const long long groups = static_cast<long long>(n) * k * (ldy / 4);
-    conv_pack_grad_kernel<<<static_cast<int>(std::min<long long>((groups + 255) / 256, 148LL * 8)), 256, 0, stream>>>(
-        dy, k, P, Q, wp, ldy, groups, g_hi, g_lo);
+    const long long grad_rows = static_cast<long long>(n) * k;
+    dim3 ggrid(static_cast<unsigned>((ldy / 4 + 127) / 128), static_cast<unsigned>(std::min(grad_rows, 148LL * 16)));
+    conv_pack_grad_kernel<<<ggrid, 128, 0, stream>>>(dy, P, Q, wp, ldy, grad_rows,
+                                                     make_fastdiv(static_cast<uint32_t>(wp)), g_hi, g_lo);
     MFB_CUDA_TRY(cudaGetLastError(), "wgrad gradient prepass launch");
 
     CUtensorMap map_a, map_b;
