@@ -53,6 +53,7 @@ SHAPES = [
     (2, 32, 20, 20, 48, 3, 3, 1, 0),     # pad 0: input-gradient padding R - 1 = 2
     (64, 32, 12, 12, 64, 1, 1, 1, 0),    # 1x1
     (52, 48, 24, 24, 40, 3, 3, 1, 1),    # 48 channels: the input gradient's conv has 48 "filters"
+    (4, 3, 32, 32, 64, 7, 7, 1, 3),      # 7x7, 3 channels: 49 taps of one 32-row group each (13 row tiles)
     (2, 6, 11, 9, 5, 3, 3, 2, 1),        # stride 2: direct kernels
     (1, 3, 8, 8, 4, 3, 3, 1, 1),         # tiny: direct kernels
 ]

@@ -161,7 +161,10 @@ def test_conv_known_answers():
     (8, 7, 33, 31, 40, 3, 3, 1, 1), (8, 33, 17, 15, 48, 3, 1, 1, 1), (64, 32, 20, 20, 64, 1, 1, 1, 0),
     (3, 5, 45, 37, 19, 5, 5, 1, 2),
     # many stacked-B tiles per SM; the second case leaves most of each image's last tile empty
-    (40, 20, 30, 30, 64, 3, 3, 1, 1), (150, 33, 17, 15, 48, 3, 3, 1, 1)])
+    (40, 20, 30, 30, 64, 3, 3, 1, 1), (150, 33, 17, 15, 48, 3, 3, 1, 1),
+    # 7x7 stem (49 taps, one channel slab each); 96 channels = 3 slabs per tap, so two-slab K blocks
+    # straddle taps
+    (8, 3, 64, 64, 64, 7, 7, 1, 3), (4, 96, 20, 20, 64, 3, 3, 1, 1)])
 def test_conv_seeded_against_restatement(n, c, h, w, k, r, s, stride, pad):
     x = oracle.seeded((n, c, h, w), seed=c)
     wt = oracle.seeded((k, c, r, s), "normal", seed=k, scale=float(np.sqrt(2.0 / (c * r * s))))
