@@ -8,7 +8,7 @@ import torch
 
 import matrixflash_pro_b200 as mf
 import oracle
-from helpers import assert_strict, to_dev
+from helpers import assert_strict, assert_tf32, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -174,6 +174,19 @@ def test_conv_seeded_against_restatement(n, c, h, w, k, r, s, stride, pad):
     ref64 = oracle.conv2d_f64(x, wt, bias, stride, pad)
     assert oracle.normwise_rel(got, ref64) <= max(1e-6, oracle.normwise_rel(ref, ref64))
     assert oracle.max_abs(got, ref) <= 1e-5 * c * r * s * float(np.abs(x).max() * np.abs(wt).max())
+
+
+# TF32 tiles: 16/32/64 filters take four 32-channel slabs per K block, which straddle taps when
+# the channels fill 1, 2 or 3 slabs per tap; 128 and 256 filters take one slab.
+@pytest.mark.parametrize("n,c,h,w,k,r,s,pad", [
+    (8, 16, 20, 20, 24, 3, 3, 1), (8, 40, 18, 18, 32, 3, 3, 1), (4, 96, 20, 20, 64, 3, 3, 1),
+    (8, 3, 64, 64, 64, 7, 7, 3), (2, 64, 20, 20, 128, 3, 3, 1), (2, 32, 14, 14, 200, 3, 3, 1)])
+def test_conv_tf32_seeded(n, c, h, w, k, r, s, pad):
+    x = oracle.seeded((n, c, h, w), seed=c + 1)
+    wt = oracle.seeded((k, c, r, s), "normal", seed=k + 1, scale=float(np.sqrt(2.0 / (c * r * s))))
+    bias = oracle.seeded((k,), "normal", seed=5, scale=0.1)
+    got = mf.conv2d(to_dev(x), to_dev(wt), to_dev(bias), 1, pad, mf.GemmPrecision.tf32).cpu().numpy()
+    assert_tf32(got, oracle.conv2d_f32(x, wt, bias, 1, pad), f"conv tf32 {(n, c, h, w, k, r, s)}")
 
 
 @pytest.mark.slow
