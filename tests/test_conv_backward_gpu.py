@@ -79,14 +79,16 @@ def test_backward_against_oracle(shape):
     _gate(db, db32, db64, n * p * q, float(np.abs(g).max()), 1.0, f"db {shape}")
 
 
-def test_tf32_precision():
-    shape = (4, 64, 28, 28, 64, 3, 3, 1, 1)
+@pytest.mark.parametrize("shape", [(4, 64, 28, 28, 64, 3, 3, 1, 1), (4, 96, 20, 20, 40, 3, 3, 1, 1),
+                                   (4, 3, 32, 32, 64, 7, 7, 1, 3)])
+def test_tf32_precision(shape):
+    pad = shape[8]
     x, wt, g = _inputs(*shape, seed=3)
     X, W, G = to_dev(x), to_dev(wt), to_dev(g)
-    dx = mf.conv2d_input_backward(G, X, W, 1, 1, TF32).cpu().numpy()
-    assert oracle.normwise_rel(dx, oracle.conv2d_input_backward(g, wt, x.shape, 1, 1)) <= 5e-3
-    dw = mf.conv2d_weight_backward(G, X, W, 1, 1, TF32).cpu().numpy()
-    assert oracle.normwise_rel(dw, oracle.conv2d_weight_backward(g, x, wt.shape, 1, 1)) <= 5e-3
+    dx = mf.conv2d_input_backward(G, X, W, 1, pad, TF32).cpu().numpy()
+    assert oracle.normwise_rel(dx, oracle.conv2d_input_backward(g, wt, x.shape, 1, pad)) <= 5e-3
+    dw = mf.conv2d_weight_backward(G, X, W, 1, pad, TF32).cpu().numpy()
+    assert oracle.normwise_rel(dw, oracle.conv2d_weight_backward(g, x, wt.shape, 1, pad)) <= 5e-3
 
 
 def test_full_size_sampled():
