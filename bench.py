@@ -238,6 +238,79 @@ def run_reference_arm(args, wl):
     return 0
 
 
+class SampledCheck:
+    """Oracle check of one seeded 64 x 64 block of this rank's C, run after the timed region
+    (the reference's benchmark validates its timed product the same way,
+    benchmarks/bench_gemm_fair.cpp:76-95,153,157).
+
+    Before the first step it keeps C's starting values on the sampled rows. After the timed
+    steps it writes them back, makes every rank but the broadcast root forget B (NaN), runs
+    one more step of the same operator (so the sampled columns of B reach this rank through
+    the broadcast) and compares the block with the oracle's gemm_f32 on the same inputs and
+    with an FP64 product. Gates: strict FP32 ||C - C64||_F / ||C64||_F <= max(1e-6, that
+    error of gemm_f32 itself) and max |C - C_gemm_f32| <= 1e-5 k max|A| max|B|; TF32
+    ||C - C_gemm_f32||_F / ||C_gemm_f32||_F <= 5e-3."""
+
+    SIZE = 64
+
+    def __init__(self, torch, m, n, k, C, rank):
+        rng = np.random.default_rng(20261001 + rank)
+        self.rows = np.sort(rng.choice(m, size=min(self.SIZE, m), replace=False))
+        # the sampled columns are the same on every rank
+        self.cols = np.sort(np.random.default_rng(20261001).choice(n, size=min(self.SIZE, n), replace=False))
+        self.rows_dev = torch.from_numpy(self.rows).to(C.device)
+        self.cols_dev = torch.from_numpy(self.cols).to(C.device)
+        self.c0_rows = C.index_select(0, self.rows_dev).clone()  # (rows, n) on the device
+        self.k = k
+
+    def run(self, torch, op, A, B, B_buf, C, alpha, beta, strict, rank, src=0):
+        import oracle
+        C.index_copy_(0, self.rows_dev, self.c0_rows)
+        a_s = A.index_select(0, self.rows_dev).cpu().numpy()                      # (64, k)
+        b_s = B.index_select(1, self.cols_dev).cpu().numpy()                      # (k, 64)
+        c0 = self.c0_rows.index_select(1, self.cols_dev).cpu().numpy()            # (64, 64)
+        if rank != src:
+            B_buf.fill_(float("nan"))  # only the broadcast can bring B to this rank
+        if C.is_cuda:
+            torch.cuda.synchronize()
+        op(A, B, C, alpha, beta)
+        if C.is_cuda:
+            torch.cuda.synchronize()
+        got = C.index_select(0, self.rows_dev).index_select(1, self.cols_dev).cpu().numpy()
+        r, s = a_s.shape[0], b_s.shape[1]
+        ref32 = oracle.gemm_f32_sampled(np.arange(r), np.arange(s), s, self.k, a_s, self.k, np.ascontiguousarray(b_s),
+                                        s, c_in=c0, alpha=alpha, beta=beta)
+        ref64 = alpha * (a_s.astype(np.float64) @ b_s.astype(np.float64))
+        if beta != 0.0:
+            ref64 += beta * c0.astype(np.float64)
+        finite = bool(np.isfinite(got).all())
+        max_abs = oracle.max_abs(got, ref32) if finite else float("inf")
+        if strict:
+            err = oracle.normwise_rel(got, ref64) if finite else float("inf")
+            oracle_err = oracle.normwise_rel(ref32, ref64)
+            gate = max(1e-6, oracle_err)
+            bound = oracle.elementwise_bound(self.k, float(np.abs(a_s).max()), float(np.abs(b_s).max()))
+            ok = finite and err <= gate and max_abs <= bound
+        else:
+            err = oracle.normwise_rel(got, ref32) if finite else float("inf")
+            oracle_err = oracle.normwise_rel(ref32, ref64)
+            gate, bound = 5e-3, float("inf")
+            ok = finite and err <= gate
+        return [err, gate, max_abs, bound, oracle_err, 1.0 if ok else 0.0]
+
+    @staticmethod
+    def summarize(per_rank, strict):
+        """Worst rank of the per-rank results (lists from run())."""
+        worst = max(range(len(per_rank)), key=lambda i: (per_rank[i][5] == 0.0, per_rank[i][0] / per_rank[i][1]))
+        err, gate, max_abs, bound, oracle_err, _ = per_rank[worst]
+        return {"ok": all(r[5] == 1.0 for r in per_rank), "ranks": len(per_rank), "worst_rank": worst,
+                "normwise": err, "normwise_vs": "fp64" if strict else "gemm_f32", "gate": gate,
+                "max_abs_vs_gemm_f32": max_abs, "elementwise_bound": bound if strict else None,
+                "gemm_f32_vs_fp64": oracle_err,
+                "block": "64 seeded rows of each rank x 64 seeded columns, after the timed steps, one more step "
+                         "from C's starting values with B known only to the broadcast root"}
+
+
 AUX_WORKLOADS = {
     # GEMV / skinny GEMM: A 16384 x 16384 ~ U[-1,1], x 16384 x n ~ N(0,1), alpha 1, beta 0.
     "gemv_n1": ("gemv", 1), "gemv_n4": ("gemv", 4), "gemv_n8": ("gemv", 8), "gemv_n16": ("gemv", 16),
@@ -575,6 +648,7 @@ def main():
     ap.add_argument("--precision", choices=["fp32", "tf32"], default="fp32")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true", help="skip the oracle check of a sampled block of C")
     ap.add_argument("--ref-rows", type=int, default=2048, help="rows per reference-arm step (bounded sample)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -618,6 +692,7 @@ def main():
     C_buf = torch.randn((m, ldc), device="cuda", generator=gen)
     A, B, C = A_buf[:, :k], B_buf[:, :n], C_buf[:, :n]
     op = RowSplitGemm(m, n, k, lda, ldb, ldc, precision)
+    check = SampledCheck(torch, m, n, k, C, rank) if not args.no_check else None
 
     def barrier():
         if world > 1:
@@ -717,9 +792,25 @@ def main():
                        + ("" if world == 1 else "; B copied in on rank 0 and broadcast (NCCL)"),
                "link": link_roofline(torch, h2d, d2h, e2e_ms / args.e2e_steps)}
 
+    # ---------------------------------------------------------------- oracle check (every rank)
+    strict = precision == mf.GemmPrecision.fp32
+    check_line = None
+    if check is not None:
+        try:
+            res = check.run(torch, op, A, B, B_buf, C, alpha, beta, strict, rank)
+        except Exception as exc:  # reported as a failed check; every rank still joins the gather
+            print(f"rank {rank}: oracle check failed to run: {exc}", file=sys.stderr)
+            res = [float("inf"), 0.0, float("inf"), 0.0, float("nan"), 0.0]
+        mine = torch.tensor(res, device="cuda", dtype=torch.float64)
+        if world > 1:
+            gathered = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(gathered, mine)
+        else:
+            gathered = [mine]
+        check_line = SampledCheck.summarize([g.cpu().tolist() for g in gathered], strict)
+
     # ---------------------------------------------------------------- roofline of the GEMM kernel
     peaks, peak_src = read_peaks()
-    strict = precision == mf.GemmPrecision.fp32
     passes = 6.0 if strict else 2.0   # TF32 runs at half the bf16 rate; strict = 3 TF32 passes
     # Short loops of ~3-5 ms steps run at full clocks (see "clocks"): burst denominator. Long steps
     # (the 32768^3 case: ~0.4 s each, seconds in total) run into the 1000 W power cap: sustained.
@@ -775,13 +866,16 @@ def main():
                               f"step footprint {footprint / 2**20:.0f} MiB, larger than L2 (126 MB) every step"),
                        "global_batch": m * world, "seq_len": None},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": op.launches_per_step() * args.steps, "clocks": clk,
+            "gpu_launches": op.launches_per_step() * args.steps, "clocks": clk, "check": check_line,
         }
         print(json.dumps(line))
     op.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    if check_line is not None and not check_line["ok"]:
+        print(f"oracle check failed: {check_line}", file=sys.stderr)
+        return 3
     return 0
 
 

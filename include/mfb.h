@@ -164,8 +164,12 @@ MFB_API mfb_status_t mfb_sgemm_strided_batched(int device, mfb_stream_t stream, 
  * static device array of MFB_NOALLOC_SCRATCH_BYTES (64 MiB, e.g. a 2048^3 strict GEMM)
  * that every GPU loading the library holds until exit; larger problems return
  * MFB_EINVAL. The first call on a device looks up the array's address
- * (cudaGetSymbolAddress); make it before any stream capture. All calls share the array:
- * calls that overlap on the GPU race, so order them on one stream. */
+ * (cudaGetSymbolAddress) and caches it for the device's current CUDA context; make that
+ * call before any stream capture, and again after a device reset (a new context looks the
+ * address up once more). All calls share the array and it keeps the last call's contents
+ * (nothing in it needs to start at zero: the operand prepass rewrites all that the GEMM
+ * reads): calls that overlap on the GPU race, so order them on one stream. Unlike
+ * mfb_sgemm, vectors (n <= 16 or m == 1) also run the tcgen05 GEMM here. */
 #define MFB_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
 MFB_API mfb_status_t mfb_sgemm_noalloc(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
                                        const float* b, float* c, const float* bias);
@@ -183,6 +187,9 @@ typedef struct mfb_plan_info {
     size_t workspace_bytes;/* device scratch owned by the plan */
     char kernel[64];       /* kernel family name */
     int sm_pair;           /* 1: 256-row tiles on SM pairs (tcgen05.mma.cta_group::2) */
+    int split_k;           /* most persistent workers that share one tile's K range (1: no split) */
+    int stream_k_tiles;    /* tiles whose K range is shared (stream-K), summed by a fix-up kernel */
+    int workers;           /* persistent CTAs (or SM pairs) of one launch */
 } mfb_plan_info;
 
 /* Builds tile choice, scratch and launch state for one problem on `device`.
@@ -217,6 +224,10 @@ MFB_API mfb_status_t mfb_plan_set_sm_limit(mfb_plan_t plan, int sms);
  * of the plan; c is never touched), keeps the fastest, and reports it. Synchronizes. */
 MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream, const float* a, const float* b,
                                    float* scratch_c, int repeats, int* candidates_tested, float* best_ms);
+/* Makes candidate `index` (0 = the plan's own first choice, < info.candidates) the
+ * configuration execute uses, as mfb_plan_tune does with the fastest one; for callers that
+ * keep their own tuning results. No reference counterpart. */
+MFB_API mfb_status_t mfb_plan_select_candidate(mfb_plan_t plan, int index);
 MFB_API mfb_status_t mfb_plan_info_get(mfb_plan_t plan, mfb_plan_info* info);
 MFB_API mfb_status_t mfb_plan_destroy(mfb_plan_t plan);
 

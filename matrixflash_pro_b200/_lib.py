@@ -22,7 +22,7 @@ EXPORTED_SYMBOLS = (
     "mfb_sgemm_noalloc", "mfb_sgemm_strided_batched",
     "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_prepare_cols",
     "mfb_plan_multiply_cols", "mfb_plan_set_sm_limit",
-    "mfb_plan_tune", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
+    "mfb_plan_tune", "mfb_plan_select_candidate", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
     "mfb_conv2d_fwd", "mfb_naive_sgemm", "mfb_probe_wait_timeout", "mfb_covariance", "mfb_correlation",
     "mfb_probe_tf32_mma_tflops", "mfb_conv2d_bwd_data", "mfb_conv2d_bwd_filter", "mfb_conv2d_bwd_bias",
     "mfb_all_reduce", "mfb_broadcast", "mfb_all_gather", "mfb_reduce_scatter", "mfb_scatter", "mfb_gather",
@@ -49,7 +49,8 @@ class PlanInfo(ctypes.Structure):
                 ("trans_a", ctypes.c_int), ("trans_b", ctypes.c_int), ("epilogue", ctypes.c_int),
                 ("path", ctypes.c_int), ("tile_n", ctypes.c_int), ("stages", ctypes.c_int),
                 ("candidates", ctypes.c_int), ("workspace_bytes", ctypes.c_size_t), ("kernel", ctypes.c_char * 64),
-                ("sm_pair", ctypes.c_int)]
+                ("sm_pair", ctypes.c_int), ("split_k", ctypes.c_int), ("stream_k_tiles", ctypes.c_int),
+                ("workers", ctypes.c_int)]
 
 
 _vp = ctypes.c_void_p
@@ -102,6 +103,7 @@ def _declare(lib):
         "mfb_plan_set_sm_limit": (st, [_vp, ctypes.c_int]),
         "mfb_plan_tune": (st, [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                ctypes.POINTER(ctypes.c_float)]),
+        "mfb_plan_select_candidate": (st, [_vp, ctypes.c_int]),
         "mfb_plan_info_get": (st, [_vp, ctypes.POINTER(PlanInfo)]),
         "mfb_plan_destroy": (st, [_vp]),
         "mfb_gemv": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),

@@ -111,6 +111,48 @@ __global__ void scale_epilogue_kernel(float* __restrict__ c, long long ldc, int 
     }
 }
 
+// Stream-K fix-up: every tile whose K blocks were shared by several workers (see
+// TcWorkIter) is the sum of its partial slots, added in K order (worker order), then
+// written through the GEMM's own store (alpha, beta * C, bias, activation). Tiles that one
+// worker covered whole were written by the GEMM and are skipped. blockIdx.y = stream-K
+// tile; the x blocks cover its ROWS x BN values four at a time.
+template <class Prob, int ROWS>
+__global__ void __launch_bounds__(256) streamk_reduce_kernel(const GemmTcParams p, int workers) {
+    grid_dependency_wait();  // the GEMM's partial sums (programmatic launch)
+    constexpr int BN = Prob::BN;
+    const int r = blockIdx.y;
+    const int kb = p.num_kb;
+    const long long iters = static_cast<long long>(p.sk_tiles) * kb;
+    const int w0 = tc_sk_owner(static_cast<long long>(r) * kb, iters, workers);
+    const int w1 = tc_sk_owner(static_cast<long long>(r + 1) * kb - 1, iters, workers);
+    if (w0 == w1) return;
+    const typename Prob::Tile t = Prob::tile(p, Prob::num_tiles(p) - p.sk_tiles + r);
+    using Store = GemmProblem<BN, 1, 1, 0, 1>;
+    const typename Store::Tile st{t.m0, t.n0, t.b};
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < ROWS * BN / 4; g += gridDim.x * blockDim.x) {
+        const int row = g / (BN / 4);
+        const int col = (g - row * (BN / 4)) * 4;
+        if (t.m0 + row >= p.m || t.n0 + col >= p.n) continue;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = w0; w <= w1; ++w) {
+            const long long first_rel = (iters * w / workers) / kb;
+            const int slot = r == first_rel ? 2 * w : 2 * w + 1;
+            const float4 v = *reinterpret_cast<const float4*>(
+                p.partials + static_cast<long long>(slot) * (ROWS * BN) + static_cast<long long>(row) * BN + col);
+            if (w == w0) {
+                acc = v;
+            } else {
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+        }
+        const float out[4] = {acc.x, acc.y, acc.z, acc.w};
+        Store::template store<4>(p, st, row, col, out);
+    }
+}
+
 // ------------------------------------------------------------------------------------
 // TMA descriptors
 // ------------------------------------------------------------------------------------
@@ -199,6 +241,7 @@ struct TcEntry {
     int threads;
     int pair;  // SM-pair kernel (cluster of 2, 256-row tiles)
     int kslabs;  // 32-deep K slabs per stage (the kernel's K block is 32 * kslabs deep)
+    const void* reduce;  // stream-K fix-up kernel for this tile shape
 };
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN, int KS = 1>
@@ -206,7 +249,7 @@ TcEntry make_entry() {
     using P = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN, KS>;
     using L = TcLayout<P>;
     return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_persistent_kernel<P>), L::kBytes,
-                   L::kThreads, 0, KS};
+                   L::kThreads, 0, KS, reinterpret_cast<const void*>(&streamk_reduce_kernel<P, kTcBM>)};
 }
 
 template <int BN, int STAGES, int PLANES, int A_MN, int B_MN, int KS = 1>
@@ -214,7 +257,7 @@ TcEntry make_pair_entry() {
     using P = GemmPairProblem<BN, STAGES, PLANES, A_MN, B_MN, KS>;
     using L = TcPairLayout<P>;
     return TcEntry{BN, STAGES, PLANES, A_MN, B_MN, reinterpret_cast<const void*>(&tc_pair_kernel<P>), L::kBytes,
-                   L::kThreads, 1, KS};
+                   L::kThreads, 1, KS, reinterpret_cast<const void*>(&streamk_reduce_kernel<P, 2 * kTcBM>)};
 }
 
 const TcEntry* kernel_table(int* count) {
@@ -290,44 +333,185 @@ size_t plane_floats(int rows, int cols) {
 // ------------------------------------------------------------------------------------
 // Configuration choice
 // ------------------------------------------------------------------------------------
+namespace {
+
+// Serialized: the attributes are per kernel, and concurrent host threads launch the same ones.
+std::mutex g_attr_mutex;
+
+mfb_status_t set_kernel_attributes(const TcEntry* e) {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem),
+                 "cudaFuncSetAttribute(max dynamic smem)");
+    if (e->pair)
+        MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 0),
+                     "cudaFuncSetAttribute(cluster size)");
+    return MFB_OK;
+}
+
+// Clusters of 2 CTAs of the pair kernel `e` that can be co-resident on `dev` (queried once).
+mfb_status_t pair_capacity(const TcEntry* e, int dev, int* out) {
+    static std::mutex mutex;
+    static std::map<std::pair<int, const void*>, int> cache;
+    {
+        std::lock_guard<std::mutex> lock(mutex);
+        auto it = cache.find({dev, e->fn});
+        if (it != cache.end()) {
+            *out = it->second;
+            return MFB_OK;
+        }
+    }
+    MFB_TRY(set_kernel_attributes(e));
+    cudaLaunchConfig_t lc{};
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    lc.gridDim = dim3(static_cast<unsigned>(2 * (sm_count(dev) / 2)));
+    lc.blockDim = dim3(e->threads);
+    lc.dynamicSmemBytes = static_cast<size_t>(e->smem);
+    lc.attrs = &attr;
+    lc.numAttrs = 1;
+    int n = 0;
+    MFB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, e->fn, &lc), "cudaOccupancyMaxActiveClusters");
+    if (n <= 0) return fail(MFB_EUNSUPPORTED, "no SM pair can host the pair GEMM kernel");
+    std::lock_guard<std::mutex> lock(mutex);
+    cache[{dev, e->fn}] = n;
+    *out = n;
+    return MFB_OK;
+}
+
+// Persistent workers of a launch of `e`: one per SM (single-CTA tiles) or per co-resident SM
+// pair, within the caller's SM limit.
+mfb_status_t worker_count(const TcEntry* e, int dev, int sm_limit, int* out) {
+    const int sms = sm_limit > 0 ? std::min(sm_limit, sm_count(dev)) : sm_count(dev);
+    if (!e->pair) {
+        *out = std::max(1, sms);
+        return MFB_OK;
+    }
+    int cap = 0;
+    MFB_TRY(pair_capacity(e, dev, &cap));
+    *out = std::max(1, std::min(cap, sms / 2));
+    return MFB_OK;
+}
+
+// Stream-K share of a launch: how many of the last tiles split their K blocks among all
+// workers (0: every tile data parallel). Whole tiles are dealt out while that keeps at least
+// 90% of the workers busy in the last wave; otherwise the last one or two waves' worth of
+// tiles (all tiles when there is less than one wave) are shared, provided every worker
+// still gets at least kMinSkBlocks K blocks (shorter shares would spend more on filling the
+// pipeline and on the fix-up than they save). The reference's GemmPlan leaves this to
+// cuBLASLt's heuristic (src/ops/gemm/plan/implementation.inc:13-60).
+constexpr int kMinSkBlocks = 8;
+
+long long streamk_tiles(long long tiles, int workers, int kb) {
+    if (workers <= 1 || tiles <= 0 || kb <= 0) return 0;
+    const long long waves = (tiles + workers - 1) / workers;
+    if (tiles * 10 >= waves * workers * 9) return 0;
+    const long long full = tiles / workers;
+    const long long sk = full >= 1 ? tiles - (full - 1) * workers : tiles;
+    if (sk * kb < static_cast<long long>(kMinSkBlocks) * workers) return 0;
+    return sk;
+}
+
+// Most workers that share one stream-K tile.
+int streamk_split(long long sk_tiles, int kb, int workers) {
+    const long long iters = sk_tiles * kb;
+    int most = 1;
+    for (long long r = 0; r < sk_tiles; ++r)
+        most = std::max(most, tc_sk_owner((r + 1) * kb - 1, iters, workers) - tc_sk_owner(r * kb, iters, workers) + 1);
+    return most;
+}
+
+long long tile_count(const mfb_gemm_desc& d, const TcEntry& e, int n_cols, int batch) {
+    const int rows = e.pair ? 2 * kTcBM : kTcBM;
+    return static_cast<long long>(batch) * ((d.m + rows - 1) / rows) * ((n_cols + e.bn - 1) / e.bn);
+}
+
+int kb_count(const mfb_gemm_desc& d, const TcEntry& e) { return (d.k + kBK * e.kslabs - 1) / (kBK * e.kslabs); }
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------
+// Configuration choice
+// ------------------------------------------------------------------------------------
 int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch) {
     const int planes = d.precision == MFB_PRECISION_TF32 ? 1 : 2;
     const int a_mn = d.trans_a ? 1 : 0;
     const int b_mn = d.trans_b ? 0 : 1;
     int count = 0;
     const TcEntry* t = kernel_table(&count);
-    const int sms = 148;
-    const long long tiles_m = (d.m + kTcBM - 1) / kTcBM;
-    // Widest tile that still fills the GPU goes first; the rest follow by width.
-    int order[16];
-    int n_ok = 0;
-    for (int i = 0; i < count && n_ok < 16; ++i)
-        if (t[i].planes == planes && t[i].a_mn == a_mn && t[i].b_mn == b_mn)
-            order[n_ok++] = i;
-    // SM pairs first when they fill the GPU (their 256-row tiles halve B's shared-memory
-    // traffic per FLOP), then the widest single-CTA tile that fills it, then narrower ones.
-    std::sort(order, order + n_ok, [&](int x, int y) {
-        auto score = [&](int idx) {
-            const long long rows = t[idx].pair ? (d.m + 2 * kTcBM - 1) / (2 * kTcBM) : tiles_m;
-            const long long tiles = batch * rows * ((d.n + t[idx].bn - 1) / t[idx].bn);
-            const long long slots = t[idx].pair ? sms / 2 : sms;
-            const bool fills = tiles >= (slots * 4) / 5;
-            return (fills ? 1000 : 0) + (fills && t[idx].pair ? 500 : 0) + (fills ? t[idx].bn : -t[idx].bn);
-        };
-        return score(x) > score(y);
-    });
-    int n_out = 0;
-    for (int i = 0; i < n_ok && n_out < max_out; ++i) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = sm_count(dev);
+    // Estimated rate of each admissible kernel, as or without a stream-K launch: the tile
+    // shape's per-SM rate (measured order: SM-pair 256 x 256 tiles, which halve B's
+    // shared-memory traffic per FLOP, then 128 x 256, 128 x 128, 128 x 64) times the share of
+    // workers that stay busy (whole waves of tiles, or ~95% with a stream-K share).
+    struct Scored {
         TcConfig c;
-        c.bn = t[order[i]].bn;
-        c.stages = t[order[i]].stages;
+        double score;
+    };
+    Scored all[32];
+    int n_all = 0;
+    for (int i = 0; i < count && n_all < 31; ++i) {
+        const TcEntry& e = t[i];
+        if (e.planes != planes || e.a_mn != a_mn || e.b_mn != b_mn) continue;
+        const double rate = e.pair ? 1.0 : e.bn >= 256 ? 0.93 : e.bn >= 128 ? 0.8 : 0.6;
+        const int workers = std::max(1, e.pair ? sms / 2 : sms);
+        const long long tiles = tile_count(d, e, d.n, batch);
+        const long long waves = (tiles + workers - 1) / workers;
+        const double busy = waves > 0 ? static_cast<double>(tiles) / static_cast<double>(waves * workers) : 0.0;
+        TcConfig c;
+        c.bn = e.bn;
+        c.stages = e.stages;
         c.planes = planes;
         c.a_mn = a_mn;
         c.b_mn = b_mn;
-        c.pair = t[order[i]].pair;
-        out[n_out++] = c;
+        c.pair = e.pair;
+        c.stream_k = 0;
+        all[n_all++] = Scored{c, rate * busy};
+        if (streamk_tiles(tiles, workers, kb_count(d, e)) > 0) {
+            c.stream_k = 1;
+            all[n_all++] = Scored{c, rate * std::max(busy, 0.95)};
+        }
     }
+    std::stable_sort(all, all + n_all, [](const Scored& x, const Scored& y) { return x.score > y.score; });
+    int n_out = 0;
+    for (int i = 0; i < n_all && n_out < max_out; ++i) out[n_out++] = all[i].c;
     return n_out;
+}
+
+mfb_status_t tc_schedule(const mfb_gemm_desc& d, const TcConfig& cfg, int dev, int sm_limit, int batch,
+                         int n_cols, TcSchedule* out) {
+    const TcEntry* e = find_kernel(cfg);
+    if (!e) return fail(MFB_EUNSUPPORTED, "no tcgen05 kernel for this tile configuration");
+    TcSchedule sc;
+    sc.tiles = tile_count(d, *e, n_cols, batch);
+    sc.kb = kb_count(d, *e);
+    MFB_TRY(worker_count(e, dev, sm_limit, &sc.workers));
+    sc.sk_tiles = cfg.stream_k ? static_cast<int>(streamk_tiles(sc.tiles, sc.workers, sc.kb)) : 0;
+    if (sc.sk_tiles > 0) {
+        sc.split = streamk_split(sc.sk_tiles, sc.kb, sc.workers);
+        sc.partial_bytes = 2ull * static_cast<size_t>(sc.workers) * static_cast<size_t>(e->pair ? 2 * kTcBM : kTcBM) *
+                           static_cast<size_t>(e->bn) * 4u;
+    }
+    *out = sc;
+    return MFB_OK;
+}
+
+size_t tc_workspace_bytes_for(const mfb_gemm_desc& d, const TcConfig& cfg, int batch) {
+    size_t bytes = round_up(static_cast<long long>(tc_workspace_bytes(d, batch)), 256);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    TcSchedule sc;
+    if (cfg.stream_k) {
+        if (tc_schedule(d, cfg, dev, 0, batch, d.n, &sc) == MFB_OK)
+            bytes += sc.partial_bytes;
+        else
+            clear_error();  // sized without a stream-K share; the launch then runs data parallel
+    }
+    return bytes;
 }
 
 size_t tc_workspace_bytes(const mfb_gemm_desc& d, int batch) {
@@ -475,69 +659,63 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     if (tiles > 0x7fffffffLL) return fail(MFB_EINVAL, "problem has too many output tiles");
     int dev = 0;
     cudaGetDevice(&dev);
-    // Persistent: one CTA per SM, or fewer when the caller leaves SMs to a concurrent collective.
-    const int sms = sm_limit > 0 ? std::min(sm_limit, sm_count(dev)) : sm_count(dev);
-    static std::mutex attr_mutex;
-    {
-        std::lock_guard<std::mutex> lock(attr_mutex);
-        MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->smem),
-                     "cudaFuncSetAttribute(max dynamic smem)");
-        if (e->pair)
-            MFB_CUDA_TRY(cudaFuncSetAttribute(e->fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 0),
-                         "cudaFuncSetAttribute(cluster size)");
+    // Persistent: one CTA per SM (or SM pair), or fewer when the caller leaves SMs to a
+    // concurrent collective. A stream-K launch keeps every worker; its partial slots follow
+    // the operand planes in the workspace (column-range calls stay data parallel).
+    TcConfig launch_cfg = cfg;
+    if (col_range) launch_cfg.stream_k = 0;
+    TcSchedule sc;
+    MFB_TRY(tc_schedule(d, launch_cfg, dev, sm_limit, nb, n1 - n0, &sc));
+    const size_t partial_off = static_cast<size_t>(round_up(static_cast<long long>(used), 256));
+    if (sc.sk_tiles > 0 && partial_off + sc.partial_bytes <= workspace_bytes) {
+        p.sk_tiles = sc.sk_tiles;
+        p.partials = reinterpret_cast<float*>(ws + partial_off);
+    } else {
+        p.sk_tiles = 0;  // no room for the partial slots: every tile data parallel
+        p.partials = nullptr;
     }
+    const long long workers = p.sk_tiles > 0 ? sc.workers : std::min<long long>(tiles, sc.workers);
+    MFB_TRY(set_kernel_attributes(e));
     void* args[] = {&map_a, &map_b, &p};
     // Right after this call's prepass the GEMM launches programmatically: its CTAs set up
     // (barriers, TMEM, descriptor prefetch) while the prepass drains, then wait for it.
     cudaLaunchAttribute pdl;
     pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl.val.programmaticStreamSerializationAllowed = 1;
-    if (!e->pair) {
-        const long long grid = std::min<long long>(tiles, sms);
-        cudaLaunchConfig_t lc{};
-        lc.gridDim = dim3(static_cast<unsigned>(grid));
-        lc.blockDim = dim3(e->threads);
-        lc.dynamicSmemBytes = static_cast<size_t>(e->smem);
-        lc.stream = stream;
-        lc.attrs = &pdl;
-        lc.numAttrs = prepass_launched ? 1 : 0;
-        MFB_CUDA_TRY(cudaLaunchKernelExC(&lc, e->fn, args), "tcgen05 GEMM launch");
-        return MFB_OK;
-    }
-    // SM pairs: clusters of 2 CTAs, as many as can be co-resident (capped by the SM limit).
     cudaLaunchConfig_t lc{};
     cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1] = pdl;
     lc.blockDim = dim3(e->threads);
     lc.dynamicSmemBytes = static_cast<size_t>(e->smem);
     lc.stream = stream;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-    // Co-resident clusters per (device, kernel), queried once.
-    static std::mutex cluster_mutex;
-    static std::map<std::pair<int, const void*>, int> cluster_cache;
-    int max_clusters = 0;
-    {
-        std::lock_guard<std::mutex> lock(cluster_mutex);
-        auto it = cluster_cache.find({dev, e->fn});
-        if (it != cluster_cache.end()) max_clusters = it->second;
+    if (!e->pair) {
+        lc.gridDim = dim3(static_cast<unsigned>(workers));
+        lc.attrs = &pdl;
+        lc.numAttrs = prepass_launched ? 1 : 0;
+        MFB_CUDA_TRY(cudaLaunchKernelExC(&lc, e->fn, args), "tcgen05 GEMM launch");
+    } else {
+        // SM pairs: clusters of 2 CTAs, as many as can be co-resident (capped by the SM limit).
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1] = pdl;
+        lc.gridDim = dim3(static_cast<unsigned>(2 * workers));
+        lc.attrs = attr;
+        lc.numAttrs = prepass_launched ? 2 : 1;
+        MFB_CUDA_TRY(cudaLaunchKernelExC(&lc, e->fn, args), "tcgen05 pair GEMM launch");
     }
-    if (max_clusters == 0) {
-        lc.gridDim = dim3(static_cast<unsigned>(2 * (sm_count(dev) / 2)));
-        MFB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, e->fn, &lc), "cudaOccupancyMaxActiveClusters");
-        if (max_clusters <= 0) return fail(MFB_EUNSUPPORTED, "no SM pair can host the pair GEMM kernel");
-        std::lock_guard<std::mutex> lock(cluster_mutex);
-        cluster_cache[{dev, e->fn}] = max_clusters;
-    }
-    const long long pairs = std::min<long long>({tiles, static_cast<long long>(max_clusters),
-                                                 static_cast<long long>(std::max(1, sms / 2))});
-    lc.gridDim = dim3(static_cast<unsigned>(2 * pairs));
-    lc.numAttrs = prepass_launched ? 2 : 1;
-    MFB_CUDA_TRY(cudaLaunchKernelExC(&lc, e->fn, args), "tcgen05 pair GEMM launch");
+    if (p.sk_tiles == 0) return MFB_OK;
+    // The fix-up of the shared tiles, launched programmatically behind the GEMM.
+    int w = static_cast<int>(sc.workers);
+    void* rargs[] = {&p, &w};
+    cudaLaunchConfig_t rc{};
+    const int per_tile = tile_rows * cfg.bn / 4;
+    rc.gridDim = dim3(static_cast<unsigned>((per_tile + 255) / 256), static_cast<unsigned>(p.sk_tiles));
+    rc.blockDim = dim3(256);
+    rc.stream = stream;
+    rc.attrs = &pdl;
+    rc.numAttrs = 1;
+    MFB_CUDA_TRY(cudaLaunchKernelExC(&rc, e->reduce, rargs), "stream-K fix-up launch");
     return MFB_OK;
 }
 

@@ -29,7 +29,21 @@ struct GemmTcParams {
     int epilogue;        // 0 none, 1 bias, 2 bias+relu, 3 bias+gelu
     int c_vec4;          // C base 16B aligned and ldc % 4 == 0
     unsigned long long wait_limit_ns;
+    int sk_tiles;        // the last sk_tiles tiles share their K blocks among the workers (stream-K)
+    float* partials;     // 2 slots per worker of (tile rows x BN) floats for shared tiles
 };
+
+// FP32 sums of a stream-K share: slot `slot` holds one tile of ROWS x BN floats, row-major;
+// CTA `rank` of an SM pair writes rows [128 rank, 128 rank + 128).
+template <int ROWS, int BN, int COUNT>
+__device__ __forceinline__ void store_partial_rows(const GemmTcParams& p, int slot, int rank, int row_in_tile,
+                                                   int col0_in_tile, const float* v) {
+    float* dst = p.partials + static_cast<long long>(slot) * (ROWS * BN) +
+                 static_cast<long long>(rank * kTcBM + row_in_tile) * BN + col0_in_tile;
+#pragma unroll
+    for (int j = 0; j < COUNT / 4; ++j)
+        reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
 
 constexpr int kBK = 32;  // 32 fp32 = 128 bytes of K per stage: one swizzle row
 
@@ -42,6 +56,7 @@ struct GemmProblem {
     static constexpr int BN = BN_, STAGES = STAGES_, PLANES = PLANES_, A_MN = A_MN_, B_MN = B_MN_;
     static constexpr int KS = KS_;
     static constexpr bool kStackB = false;  // row-major B is MN-major: its planes interleave per 32 columns
+    static constexpr bool kStreamK = true;  // p.sk_tiles / p.partials: stream-K share of the last tiles
     static constexpr int kASlabBytes = PLANES * kTcBM * kBK * 4;
     static constexpr int kBSlabBytes = PLANES * BN * kBK * 4;
     static constexpr int kATileBytes = KS * kASlabBytes;
@@ -110,6 +125,12 @@ struct GemmProblem {
     }
     __device__ static uint64_t b_desc(uint32_t addr, int pl, int ks) {
         return desc<B_MN, BN>(addr + (ks / 4) * kBSlabBytes, pl, ks % 4);
+    }
+
+    template <int COUNT>
+    __device__ static void store_partial(const Params& p, int slot, int rank, int row_in_tile, int col0_in_tile,
+                                         const float* v) {
+        store_partial_rows<kTcBM, BN, COUNT>(p, slot, rank, row_in_tile, col0_in_tile, v);
     }
 
     // Writes COUNT consecutive outputs of one row: o = epilogue(alpha * acc + beta * C).

@@ -300,7 +300,7 @@ MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream_h, const mfb_gemm
     }
     TcConfig cfgs[4];
     if (tc_candidates(d, cfgs, 4) == 0) return fail(MFB_EUNSUPPORTED, "no tcgen05 configuration");
-    const size_t need = tc_workspace_bytes(d);
+    const size_t need = tc_workspace_bytes_for(d, cfgs[0]);
     void* ws = nullptr;
     MFB_TRY(stream_workspace(device, stream, need, &ws));
     return tc_gemm(d, cfgs[0], stream, a, b, c, bias, ws, need);
@@ -343,7 +343,7 @@ MFB_API mfb_status_t mfb_sgemm_strided_batched(int device, mfb_stream_t stream_h
     batch.stride_c = stride_c;
     TcConfig cfgs[4];
     if (tc_candidates(d, cfgs, 4, batch_count) == 0) return fail(MFB_EUNSUPPORTED, "no tcgen05 configuration");
-    const size_t need = tc_workspace_bytes(d, batch_count);
+    const size_t need = tc_workspace_bytes_for(d, cfgs[0], batch_count);
     void* ws = nullptr;
     MFB_TRY(stream_workspace(device, stream, need, &ws));
     return tc_gemm(d, cfgs[0], stream, a, b, c, bias, ws, need, kPhaseAll, 0, batch);
@@ -405,7 +405,11 @@ MFB_API mfb_status_t mfb_plan_create(int device, const mfb_gemm_desc* desc, mfb_
         plan->n_candidates = tc_candidates(probe, plan->candidates, 16);
         if (plan->n_candidates == 0) return fail(MFB_EUNSUPPORTED, "no tcgen05 configuration");
         plan->cfg = plan->candidates[0];
-        need = tc_workspace_bytes(probe);  // operand planes: hi/lo (strict) or rounded TF32
+        // operand planes (hi/lo strict, or rounded TF32) and the partial slots of the largest
+        // stream-K candidate, so that tuning may pick any candidate
+        need = tc_workspace_bytes(probe);
+        for (int i = 0; i < plan->n_candidates; ++i)
+            need = std::max(need, tc_workspace_bytes_for(probe, plan->candidates[i]));
     } else if (plan->path == kPathGemv) {
         need = gemv_workspace_bytes(probe);
     }
@@ -545,6 +549,15 @@ MFB_API mfb_status_t mfb_plan_tune(mfb_plan_t plan, mfb_stream_t stream_h, const
     return MFB_OK;
 }
 
+MFB_API mfb_status_t mfb_plan_select_candidate(mfb_plan_t plan, int index) {
+    clear_error();
+    if (!plan) return fail(MFB_EINVAL, "null plan");
+    if (plan->path != kPathTc) return index == 0 ? MFB_OK : fail(MFB_EINVAL, "this plan has one candidate");
+    if (index < 0 || index >= plan->n_candidates) return fail(MFB_EINVAL, "candidate index out of range");
+    plan->cfg = plan->candidates[index];
+    return MFB_OK;
+}
+
 MFB_API mfb_status_t mfb_plan_info_get(mfb_plan_t plan, mfb_plan_info* info) {
     if (!plan || !info) return fail(MFB_EINVAL, "null plan or info");
     std::memset(info, 0, sizeof(*info));
@@ -565,6 +578,21 @@ MFB_API mfb_status_t mfb_plan_info_get(mfb_plan_t plan, mfb_plan_info* info) {
                            : plan->path == kPathGemv ? "gemv_fp32" : plan->path == kPathScale ? "scale" : "empty";
     std::snprintf(info->kernel, sizeof(info->kernel), "%s", name);
     info->sm_pair = plan->path == kPathTc ? plan->cfg.pair : 0;
+    info->split_k = 1;
+    info->stream_k_tiles = 0;
+    info->workers = 0;
+    if (plan->path == kPathTc) {
+        DeviceGuard guard;
+        MFB_TRY(select_device(plan->device));
+        TcSchedule sc;
+        MFB_TRY(tc_schedule(plan->desc, plan->cfg, plan->device, plan->sm_limit, 1, plan->desc.n, &sc));
+        const size_t planes = static_cast<size_t>((tc_workspace_bytes(plan->desc) + 255) / 256 * 256);
+        if (sc.sk_tiles > 0 && planes + sc.partial_bytes <= plan->ws_bytes) {
+            info->split_k = sc.split;
+            info->stream_k_tiles = sc.sk_tiles;
+        }
+        info->workers = sc.workers;
+    }
     return MFB_OK;
 }
 

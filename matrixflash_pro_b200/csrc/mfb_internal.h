@@ -62,6 +62,17 @@ struct TcConfig {
     int a_mn = 0;     // A stored transposed (MN-major)
     int b_mn = 1;     // B stored untransposed (MN-major)
     int pair = 0;     // 1: SM-pair kernel (cta_group::2, 256 x bn tiles)
+    int stream_k = 0; // 1: the last tiles may share their K blocks among all workers (stream-K)
+};
+
+// How one launch of a configuration spreads its tiles over the persistent workers.
+struct TcSchedule {
+    long long tiles = 0;
+    int kb = 0;              // K blocks per tile
+    int workers = 0;         // CTAs (single-CTA tiles) or SM pairs
+    int sk_tiles = 0;        // tiles whose K blocks are shared (stream-K); 0 = all data parallel
+    int split = 1;           // most workers sharing one tile
+    size_t partial_bytes = 0;  // partial slots a stream-K launch needs (2 per worker)
 };
 
 // Admissible tile configurations for a problem, best-guess first.
@@ -100,6 +111,12 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch 
 // Scratch the tcgen05 path needs for `d`: hi/lo planes of A and B (strict) or one
 // rounded TF32 plane of each (TF32), rows padded to 16 bytes.
 size_t tc_workspace_bytes(const mfb_gemm_desc& d, int batch = 1);
+// The planes (256-byte aligned) plus the partial slots of a stream-K launch of `cfg` on all
+// workers of the current device. A launch given less runs every tile data parallel.
+size_t tc_workspace_bytes_for(const mfb_gemm_desc& d, const TcConfig& cfg, int batch = 1);
+// The schedule a launch of `cfg` over n_cols output columns gets on `dev` (sm_limit as tc_gemm).
+mfb_status_t tc_schedule(const mfb_gemm_desc& d, const TcConfig& cfg, int dev, int sm_limit, int batch, int n_cols,
+                         TcSchedule* out);
 
 // Runs the tcgen05 GEMM on `stream`: kPhasePrepare launches the split/round prepass of
 // the operands into `workspace`, kPhaseMultiply the GEMM kernel on the prepared

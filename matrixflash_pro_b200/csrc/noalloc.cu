@@ -12,8 +12,11 @@
 //
 // Rules (also in include/mfb.h):
 //   * The first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (with that device current) and caches it; make that first
-//     call before any stream capture.
+//     cudaGetSymbolAddress (with that device current) and caches it under the id of the
+//     device's current CUDA context; make that first call before any stream capture. A
+//     device reset or a new primary context gets a new id, so the next call looks the
+//     address up again instead of reusing a stale one (where the driver cannot report a
+//     context id, every call looks it up).
 //   * All calls share the one array and it keeps the last call's contents. Nothing in
 //     it needs to start at zero: the prepass rewrites every element the GEMM reads.
 //     Calls that overlap on the GPU (different streams, or host threads without
@@ -23,8 +26,8 @@
 #include "gemm_tc.cuh"
 #include "mfb_internal.h"
 
+#include <map>
 #include <mutex>
-#include <vector>
 
 namespace mfb {
 
@@ -35,20 +38,54 @@ namespace {
 static __device__ __align__(256) float g_noalloc_scratch[MFB_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
 std::mutex g_noalloc_mutex;
-std::vector<void*> g_noalloc_ptrs;  // per device, resolved on the first call
+std::map<unsigned long long, void*> g_noalloc_ptrs;  // context id -> the array's device address
 
-// Must run with `device` current (select_device has made it so).
-mfb_status_t noalloc_scratch(int device, void** out) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the calling thread's current CUDA context (never reused within a process),
+// or false when the driver cannot say.
+bool current_context_id(unsigned long long* id) {
+    static CtxGetCurrentFn get_current = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    static CtxGetIdFn get_id = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<CtxGetIdFn>(p);
+    }();
+    CUcontext ctx = nullptr;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+    return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Must run with `device` current (select_device has made it so, and the runtime has made
+// its primary context current on this thread).
+mfb_status_t noalloc_scratch(void** out) {
+    unsigned long long ctx_id = 0;
+    const bool keyed = current_context_id(&ctx_id);
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (static_cast<int>(g_noalloc_ptrs.size()) <= device) g_noalloc_ptrs.resize(device + 1, nullptr);
-    if (g_noalloc_ptrs[device] == nullptr) {
-        void* ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
-        if (ptr == nullptr) return fail(MFB_ECUDA, "cudaGetSymbolAddress returned a null scratch address");
-        g_noalloc_ptrs[device] = ptr;
+    if (keyed) {
+        auto it = g_noalloc_ptrs.find(ctx_id);
+        if (it != g_noalloc_ptrs.end()) {
+            *out = it->second;
+            return MFB_OK;
+        }
     }
-    *out = g_noalloc_ptrs[device];
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    if (ptr == nullptr) return fail(MFB_ECUDA, "cudaGetSymbolAddress returned a null scratch address");
+    if (keyed) g_noalloc_ptrs[ctx_id] = ptr;
+    *out = ptr;
     return MFB_OK;
 }
 
@@ -77,6 +114,6 @@ extern "C" MFB_API mfb_status_t mfb_sgemm_noalloc(int device, mfb_stream_t strea
     TcConfig cfg[4];
     if (tc_candidates(d, cfg, 4) == 0) return fail(MFB_EUNSUPPORTED, "no tcgen05 configuration");
     void* scratch = nullptr;
-    MFB_TRY(noalloc_scratch(device, &scratch));
+    MFB_TRY(noalloc_scratch(&scratch));
     return tc_gemm(d, cfg[0], stream, a, b, c, bias, scratch, MFB_NOALLOC_SCRATCH_BYTES);
 }

@@ -71,7 +71,8 @@ CovPlan cov_plan(int rows, int cols, long long ldx, int precision, bool with_cov
     cd.precision = precision;
     cd.trans_a = 1;
     p.gemv_bytes = gemv_workspace_bytes(md);
-    p.tc_bytes = tc_workspace_bytes(cd);
+    TcConfig first[1];
+    p.tc_bytes = tc_candidates(cd, first, 1) > 0 ? tc_workspace_bytes_for(cd, first[0]) : tc_workspace_bytes(cd);
     p.ones_off = 0;
     p.mean_off = align256(static_cast<size_t>(rows) * 4);
     p.gemv_off = p.mean_off + align256(static_cast<size_t>(cols) * 4);

@@ -69,6 +69,79 @@ struct TcChunk : std::integral_constant<int, kChunkKb> {};
 template <class P>
 struct TcChunk<P, std::void_t<decltype(P::kChunkKbOverride)>> : std::integral_constant<int, P::kChunkKbOverride> {};
 
+// ------------------------------------------------------------------------------------
+// Work schedule: data-parallel tiles, then a stream-K share of the K blocks.
+//
+// Policies that declare kStreamK (the GEMM) may set p.sk_tiles > 0: the last sk_tiles
+// tiles (in the policy's raster order) are not dealt out whole; their K blocks, flattened
+// tile-major into I = sk_tiles * KB iterations, are cut into one contiguous range per
+// worker (worker w: [floor(w I / G), floor((w+1) I / G)), G workers). A tile whose K blocks
+// all fall in one worker's range is written as usual. A tile shared by several workers is
+// not: each worker stores the FP32 sum of its part in a partial slot (slot 2w for the
+// first tile of w's range, 2w + 1 for its last), and a separate reduce kernel adds a
+// tile's slots in K order and applies the epilogue, so results do not depend on timing
+// and no CTA ever waits for another. The first tiles (all but the last one or two waves)
+// stay data parallel: worker w takes tiles w, w + G, ...
+// Every role of a CTA walks the same sequence of work units.
+// ------------------------------------------------------------------------------------
+struct TcWork {
+    int tile;      // tile index in the policy's raster
+    int kb0, kb1;  // K blocks [kb0, kb1) of that tile
+    int slot;      // -1: the unit covers the whole tile (normal store); else its partial slot
+};
+
+template <class P, class = void>
+struct TcStreamK : std::false_type {};
+template <class P>
+struct TcStreamK<P, std::void_t<decltype(P::kStreamK)>> : std::integral_constant<bool, P::kStreamK> {};
+
+template <class Prob>
+__device__ __forceinline__ int tc_sk_tiles(const typename Prob::Params& p) {
+    if constexpr (TcStreamK<Prob>::value) return p.sk_tiles;
+    return 0;
+}
+
+// Worker owning flattened stream-K iteration i (the largest w with floor(w I / G) <= i).
+__host__ __device__ __forceinline__ int tc_sk_owner(long long i, long long iters, int workers) {
+    return static_cast<int>(((i + 1) * workers - 1) / iters);
+}
+
+template <class Prob>
+struct TcWorkIter {
+    int w, G, kb, dp_tiles, next_dp;
+    long long iters, i, e, first_rel;
+
+    __device__ TcWorkIter(const typename Prob::Params& p, int worker, int workers) {
+        w = worker;
+        G = workers;
+        kb = Prob::num_kb(p);
+        const int sk = tc_sk_tiles<Prob>(p);
+        dp_tiles = Prob::num_tiles(p) - sk;
+        next_dp = worker;
+        iters = static_cast<long long>(sk) * kb;
+        i = iters * worker / workers;
+        e = iters * (worker + 1) / workers;
+        first_rel = kb > 0 ? i / kb : 0;
+    }
+
+    __device__ bool next(TcWork& u) {
+        if (next_dp < dp_tiles) {
+            u = TcWork{next_dp, 0, kb, -1};
+            next_dp += G;
+            return true;
+        }
+        if (i >= e) return false;
+        const long long rel = i / kb;
+        const long long base = rel * kb;
+        const int kb0 = static_cast<int>(i - base);
+        const int kb1 = static_cast<int>(e - base < kb ? e - base : kb);
+        const bool whole = kb0 == 0 && kb1 == kb;
+        u = TcWork{dp_tiles + static_cast<int>(rel), kb0, kb1, whole ? -1 : (rel == first_rel ? 2 * w : 2 * w + 1)};
+        i = base + kb;
+        return true;
+    }
+};
+
 template <class Prob>
 struct TcLayout {
     static constexpr int kStageBytes = Prob::kATileBytes + Prob::kBTileBytes;
@@ -99,6 +172,21 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* out) {
     }
 }
 
+// Writes COUNT consecutive accumulator columns of one row of a work unit: through the
+// policy's epilogue for a whole tile (slot < 0), raw into the unit's partial slot for a
+// stream-K share (rank: the CTA's rank within an SM pair; 0 for single-CTA tiles).
+template <class Prob, int COUNT>
+__device__ __forceinline__ void tc_store(const typename Prob::Params& p, const typename Prob::Tile& tile, int slot,
+                                         int rank, int row_in_tile, int col0_in_tile, const float* v) {
+    if constexpr (TcStreamK<Prob>::value) {
+        if (slot >= 0) {
+            Prob::template store_partial<COUNT>(p, slot, rank, row_in_tile, col0_in_tile, v);
+            return;
+        }
+    }
+    Prob::template store<COUNT>(p, tile, row_in_tile, col0_in_tile, v);
+}
+
 // Epilogue role (warps 2..) shared by the persistent tcgen05 kernels: waits for each
 // finished accumulator (a tile in TF32 mode, a 64-deep K chunk in strict mode, summed in
 // registers with round-to-nearest adds), hands the TMEM buffer back to the MMA issuer and
@@ -110,15 +198,15 @@ __device__ __forceinline__ void tc_epilogue_role(const typename Prob::Params& p,
     constexpr int BN = Prob::BN;
     constexpr int PLANES = Prob::PLANES;
     constexpr int ACC = tc_acc_cols<Prob>();  // accumulator columns per buffer
-    const int num_tiles = Prob::num_tiles(p);
-    const int num_kb = Prob::num_kb(p);
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 belong to this warp
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int row = quarter * 32 + lane;  // row within the tile
     int buf = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const typename Prob::Tile tile = Prob::tile(p, t);
+    TcWorkIter<Prob> work(p, blockIdx.x, gridDim.x);
+    TcWork u;
+    while (ok && work.next(u)) {
+        const typename Prob::Tile tile = Prob::tile(p, u.tile);
         const int valid = Prob::valid_cols(p, tile);
         if constexpr (PLANES == 2) {
             // Round-to-nearest FP32 sum of the K chunks, in registers: this warp owns
@@ -129,7 +217,7 @@ __device__ __forceinline__ void tc_epilogue_role(const typename Prob::Params& p,
             float sum[kCols];
 #pragma unroll
             for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
-            const int n_chunks = (num_kb + TcChunk<Prob>::value - 1) / TcChunk<Prob>::value;
+            const int n_chunks = (u.kb1 - u.kb0 + TcChunk<Prob>::value - 1) / TcChunk<Prob>::value;
             for (int c = 0; c < n_chunks; ++c, ++buf) {
                 const int b = buf & 1;
                 if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
@@ -180,7 +268,7 @@ __device__ __forceinline__ void tc_epilogue_role(const typename Prob::Params& p,
 #pragma unroll
             for (int q = 0; q < kCols / kStep; ++q) {
                 const int col0 = half * kCols + q * kStep;
-                if (col0 < valid) Prob::template store<kStep>(p, tile, row, col0, &sum[q * kStep]);
+                if (col0 < valid) tc_store<Prob, kStep>(p, tile, u.slot, 0, row, col0, &sum[q * kStep]);
             }
         } else {
             const int b = buf & 1;
@@ -199,7 +287,7 @@ __device__ __forceinline__ void tc_epilogue_role(const typename Prob::Params& p,
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty_bar[b]);
                 }
-                Prob::template store<16>(p, tile, row, q * 16, v);
+                tc_store<Prob, 16>(p, tile, u.slot, 0, row, q * 16, v);
             }
             ++buf;
         }
@@ -227,8 +315,6 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
-    const int num_tiles = Prob::num_tiles(p);
-    const int num_kb = Prob::num_kb(p);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -263,9 +349,11 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
         // ------------------------------------------------------------ TMA producer
         int it = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-            const typename Prob::Tile tile = Prob::tile(p, t);
-            for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        TcWorkIter<Prob> work(p, blockIdx.x, gridDim.x);
+        TcWork u;
+        while (ok && work.next(u)) {
+            const typename Prob::Tile tile = Prob::tile(p, u.tile);
+            for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
                 const int s = it % STAGES;
                 if (!mbar_wait_bounded(&empty_bar[s], ((it / STAGES) & 1) ^ 1, limit, abort_flag)) {
                     report_status(kStatusTimeoutProducer, abort_flag);
@@ -293,11 +381,14 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
         int it = 0;   // K blocks consumed (stage ring position)
         int buf = 0;  // accumulator buffers used so far
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        TcWorkIter<Prob> work(p, blockIdx.x, gridDim.x);
+        TcWork u;
+        while (ok && work.next(u)) {
             uint32_t d_tmem = 0;
             uint32_t acc = 0;
-            for (int kb = 0; kb < num_kb; ++kb, ++it) {
-                if (kb % kb_per_buf == 0) {
+            for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+                const int kr = kb - u.kb0;  // K blocks into this unit
+                if (kr % kb_per_buf == 0) {
                     const int b = buf & 1;
                     if (!mbar_wait_bounded(&acc_empty_bar[b], ((buf >> 1) & 1) ^ 1, limit, abort_flag)) {
                         report_status(kStatusTimeoutMma, abort_flag);
@@ -337,7 +428,7 @@ __global__ void __launch_bounds__(TcLayout<Prob>::kThreads, 1)
                     acc = 1;
                 }
                 umma_commit(&empty_bar[s]);
-                if (kb % kb_per_buf == kb_per_buf - 1 || kb == num_kb - 1) {
+                if (kr % kb_per_buf == kb_per_buf - 1 || kb == u.kb1 - 1) {
                     umma_commit(&acc_full_bar[buf & 1]);
                     ++buf;
                 }

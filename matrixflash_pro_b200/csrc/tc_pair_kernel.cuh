@@ -43,6 +43,7 @@ struct GemmPairProblem {
     static constexpr int kBTileBytes = KS * kBSlabBytes;
     static constexpr int kKSteps = KS * kBK / 8;
     static constexpr int kPairBM = 2 * kTcBM;
+    static constexpr bool kStreamK = true;  // p.sk_tiles / p.partials: stream-K share of the last tiles
     static_assert(kBH % 32 == 0 || !B_MN, "MN-major B halves are 32-column groups");
 
     struct Tile {
@@ -51,6 +52,7 @@ struct GemmPairProblem {
     };
 
     __device__ static int num_tiles(const Params& p) { return p.batch * p.tiles_m * p.tiles_n; }
+    __device__ static int num_kb(const Params& p) { return p.num_kb; }
 
     __device__ static Tile tile(const Params& p, int t) {
         const int per_batch = p.tiles_m * p.tiles_n;
@@ -101,6 +103,22 @@ struct GemmPairProblem {
     }
 
     template <int COUNT>
+    __device__ static void store_partial(const Params& p, int slot, int rank, int row_in_tile, int col0_in_tile,
+                                         const float* v) {
+        store_partial_rows<kPairBM, BN, COUNT>(p, slot, rank, row_in_tile, col0_in_tile, v);
+    }
+
+    // Whole tile (slot < 0): the epilogue; stream-K share: the raw sum into the partial slot.
+    template <int COUNT>
+    __device__ static void store_unit(const Params& p, const Tile& t, int slot, int rank, int row_in_tile,
+                                      int col0_in_tile, const float* v) {
+        if (slot >= 0)
+            store_partial<COUNT>(p, slot, rank, row_in_tile, col0_in_tile, v);
+        else
+            store<COUNT>(p, t, rank, row_in_tile, col0_in_tile, v);
+    }
+
+    template <int COUNT>
     __device__ static void store(const Params& p, const Tile& t, int rank, int row_in_tile, int col0_in_tile,
                                  const float* v) {
         using One = GemmProblem<BN, STAGES, PLANES, A_MN, B_MN>;
@@ -147,8 +165,6 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
     const bool leader = rank == 0;
     const int pair = blockIdx.x / 2;
     const int npairs = gridDim.x / 2;
-    const int num_tiles = Prob::num_tiles(p);
-    const int num_kb = p.num_kb;
     const uint32_t abort_peer = map_to_cta(smem_u32(const_cast<int*>(abort_flag)), rank ^ 1);
 
     if (threadIdx.x == 0) {
@@ -189,9 +205,11 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
         // ------------------------------------------------------------ TMA producer (both CTAs)
         int it = 0;
         bool ok = true;
-        for (int t = pair; t < num_tiles && ok; t += npairs) {
-            const typename Prob::Tile tile = Prob::tile(p, t);
-            for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        TcWorkIter<Prob> work(p, pair, npairs);
+        TcWork u;
+        while (ok && work.next(u)) {
+            const typename Prob::Tile tile = Prob::tile(p, u.tile);
+            for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
                 const int s = it % STAGES;
                 if (!mbar_wait_bounded(&empty_bar[s], ((it / STAGES) & 1) ^ 1, limit, abort_flag)) {
                     give_up(kStatusTimeoutProducer);
@@ -218,11 +236,14 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
         int it = 0;
         int buf = 0;
         bool ok = true;
-        for (int t = pair; t < num_tiles && ok; t += npairs) {
+        TcWorkIter<Prob> work(p, pair, npairs);
+        TcWork u;
+        while (ok && work.next(u)) {
             uint32_t d_tmem = 0;
             uint32_t acc = 0;
-            for (int kb = 0; kb < num_kb; ++kb, ++it) {
-                if (kb % kb_per_buf == 0) {
+            for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+                const int kr = kb - u.kb0;  // K blocks into this unit
+                if (kr % kb_per_buf == 0) {
                     const int b = buf & 1;
                     if (!mbar_wait_bounded(&acc_empty_bar[b], ((buf >> 1) & 1) ^ 1, limit, abort_flag)) {
                         give_up(kStatusTimeoutMma);
@@ -255,7 +276,7 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
                     acc = 1;
                 }
                 umma_commit_pair(&empty_bar[s], 0x3);
-                if (kb % kb_per_buf == kb_per_buf - 1 || kb == num_kb - 1) {
+                if (kr % kb_per_buf == kb_per_buf - 1 || kb == u.kb1 - 1) {
                     umma_commit_pair(&acc_full_bar[buf & 1], 0x3);
                     ++buf;
                 }
@@ -270,8 +291,10 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
         const int row = quarter * 32 + lane;
         int buf = 0;
         bool ok = true;
-        for (int t = pair; t < num_tiles && ok; t += npairs) {
-            const typename Prob::Tile tile = Prob::tile(p, t);
+        TcWorkIter<Prob> work(p, pair, npairs);
+        TcWork u;
+        while (ok && work.next(u)) {
+            const typename Prob::Tile tile = Prob::tile(p, u.tile);
             const int valid = min(BN, p.n - tile.n0);
             if constexpr (PLANES == 2) {
                 constexpr int kCols = BN / 2;
@@ -279,7 +302,7 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
                 float sum[kCols];
 #pragma unroll
                 for (int j = 0; j < kCols; ++j) sum[j] = 0.0f;
-                const int n_chunks = (num_kb + TcChunk<Prob>::value - 1) / TcChunk<Prob>::value;
+                const int n_chunks = (u.kb1 - u.kb0 + TcChunk<Prob>::value - 1) / TcChunk<Prob>::value;
                 for (int c = 0; c < n_chunks; ++c, ++buf) {
                     const int b = buf & 1;
                     if (!mbar_wait_bounded(&acc_full_bar[b], (buf >> 1) & 1, limit, abort_flag)) {
@@ -303,7 +326,7 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
 #pragma unroll
                 for (int q = 0; q < kCols / 16; ++q) {
                     const int col0 = half * kCols + q * 16;
-                    if (col0 < valid) Prob::template store<16>(p, tile, rank, row, col0, &sum[q * 16]);
+                    if (col0 < valid) Prob::template store_unit<16>(p, tile, u.slot, rank, row, col0, &sum[q * 16]);
                 }
             } else {
                 const int b = buf & 1;
@@ -321,7 +344,7 @@ __global__ void __launch_bounds__(TcPairLayout<Prob>::kThreads, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&acc_empty_bar[b]), 0));
                     }
-                    Prob::template store<16>(p, tile, rank, row, q * 16, v);
+                    Prob::template store_unit<16>(p, tile, u.slot, rank, row, q * 16, v);
                 }
                 ++buf;
             }

@@ -140,6 +140,7 @@ class _PointerPlan:
         info = _lib.PlanInfo()
         _lib.check(_lib.lib().mfb_plan_info_get(h, ctypes.byref(info)), "row-split plan info")
         self.tcgen05 = info.path == 0
+        self.stream_k = info.stream_k_tiles > 0  # whole-matrix multiplies add a fix-up launch
 
     def set_sm_limit(self, sms: Optional[int]) -> None:
         sms = int(sms or 0)
@@ -256,10 +257,11 @@ class RowSplitGemm:
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step: on one GPU the operand prepass (hi/lo split, or TF32
-        rounding) and the GEMM; with peers A's prepass, then per column panel its B prepass and
-        its GEMM (the panel packing on rank 0 is a torch copy)."""
+        rounding), the GEMM and, when its last tiles share K among the SMs (stream-K), their
+        fix-up; with peers A's prepass, then per column panel its B prepass and its GEMM (column
+        panels stay data parallel; the panel packing on rank 0 is a torch copy)."""
         if self.world == 1 or not self.plan.tcgen05:
-            return 2
+            return 3 if self.plan.stream_k else 2
         return 1 + 2 * len(self.sched.panels)
 
     def gemm_launches_per_step(self) -> int:

@@ -317,6 +317,13 @@ class GemmPlan:
     def candidate_count(self) -> int:
         return self._candidates if self._handle else 0
 
+    def select_candidate(self, index: int) -> None:
+        """Run candidate `index` (0 = the plan's first choice) from now on, as tune() does
+        with the fastest one."""
+        if not self._handle:
+            raise InvalidArgumentError("Cannot select on a moved-from GEMM plan")
+        _lib.check(_lib.lib().mfb_plan_select_candidate(self._handle, int(index)), "plan select candidate")
+
     def uses_tcgen05(self) -> bool:
         return bool(self._handle) and self.info().path == 0
 
