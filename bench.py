@@ -43,6 +43,8 @@ WORKLOADS = {
                      "linear-layer GEMM with m=2048/GPU (profiling size; B alone exceeds L2)"),
     "square8192": (8192, 8192, 8192, 8192, 8192, 8192, 1.0, 0.0, "square GEMM 8192^3, alpha=1 beta=0"),
     "square2048": (2048, 2048, 2048, 2048, 2048, 2048, 1.0, 0.0, "square GEMM 2048^3, alpha=1 beta=0"),
+    "longk512": (512, 512, 65536, 65536, 512, 512, 1.0, 0.0,
+                 "long-K GEMM m=n=512 k=65536 (4 SM-pair tiles: K shared among the SMs), alpha=1 beta=0"),
     "c5": (32768, 32768, 32768, 32768, 32768, 32768, 1.0, 0.0,
            "square GEMM 32768^3 rows split across GPUs (32768 rows total), B broadcast"),
 }

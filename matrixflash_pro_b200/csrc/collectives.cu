@@ -237,6 +237,31 @@ mfb_status_t all_reduce_impl(const mfb_collective_buffer* ranks, int n, int op) 
 }
 
 }  // namespace
+
+mfb_status_t nccl_streams(const std::vector<int>& devices, std::vector<cudaStream_t>* streams) {
+    CommSet* set = nullptr;
+    MFB_TRY(comm_set(devices, &set));
+    *streams = set->streams;
+    return MFB_OK;
+}
+
+mfb_status_t nccl_broadcast_group(const std::vector<int>& devices, const std::vector<float*>& bufs, size_t count,
+                                  int root) {
+    CommSet* set = nullptr;
+    MFB_TRY(comm_set(devices, &set));
+    if (bufs.size() != devices.size() || root < 0 || root >= static_cast<int>(devices.size()))
+        return fail(MFB_EINVAL, "broadcast group: one buffer per device and a root among them");
+    const NcclApi& api = nccl_api();
+    MFB_NCCL_TRY(api.group_start(), "ncclGroupStart");
+    for (size_t r = 0; r < devices.size(); ++r) {
+        cudaSetDevice(devices[r]);
+        MFB_NCCL_TRY(api.broadcast(bufs[r], bufs[r], count, ncclFloat, root, set->comms[r], set->streams[r]),
+                     "ncclBroadcast");
+    }
+    MFB_NCCL_TRY(api.group_end(), "ncclGroupEnd");
+    return MFB_OK;
+}
+
 }  // namespace mfb
 
 using namespace mfb;

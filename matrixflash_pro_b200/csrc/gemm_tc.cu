@@ -115,38 +115,47 @@ __global__ void scale_epilogue_kernel(float* __restrict__ c, long long ldc, int 
 // TcWorkIter) is the sum of its partial slots, added in K order (worker order), then
 // written through the GEMM's own store (alpha, beta * C, bias, activation). Tiles that one
 // worker covered whole were written by the GEMM and are skipped. blockIdx.y = stream-K
-// tile; the x blocks cover its ROWS x BN values four at a time.
+// tile; the x blocks split its ROWS x BN values, four consecutive columns per thread step.
+// Workers w0 < w <= w1 of a shared tile r start their ranges inside it, so they hold it in
+// slot 2w; only w0 may have started in an earlier tile (slot 2 w0 + 1). Thread 0 finds
+// w0, w1 and that first slot once per block.
 template <class Prob, int ROWS>
 __global__ void __launch_bounds__(256) streamk_reduce_kernel(const GemmTcParams p, int workers) {
-    grid_dependency_wait();  // the GEMM's partial sums (programmatic launch)
     constexpr int BN = Prob::BN;
+    constexpr int kGroupsPerRow = BN / 4;
+    __shared__ int s_w0, s_w1, s_first_slot;
+    grid_dependency_wait();  // the GEMM's partial sums (programmatic launch)
     const int r = blockIdx.y;
-    const int kb = p.num_kb;
-    const long long iters = static_cast<long long>(p.sk_tiles) * kb;
-    const int w0 = tc_sk_owner(static_cast<long long>(r) * kb, iters, workers);
-    const int w1 = tc_sk_owner(static_cast<long long>(r + 1) * kb - 1, iters, workers);
+    if (threadIdx.x == 0) {
+        const int kb = p.num_kb;
+        const long long iters = static_cast<long long>(p.sk_tiles) * kb;
+        const int w0 = tc_sk_owner(static_cast<long long>(r) * kb, iters, workers);
+        s_w0 = w0;
+        s_w1 = tc_sk_owner(static_cast<long long>(r + 1) * kb - 1, iters, workers);
+        s_first_slot = (iters * w0 / workers) / kb == r ? 2 * w0 : 2 * w0 + 1;
+    }
+    __syncthreads();
+    const int w0 = s_w0, w1 = s_w1;
     if (w0 == w1) return;
+    const int first_slot = s_first_slot;
     const typename Prob::Tile t = Prob::tile(p, Prob::num_tiles(p) - p.sk_tiles + r);
     using Store = GemmProblem<BN, 1, 1, 0, 1>;
     const typename Store::Tile st{t.m0, t.n0, t.b};
-    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < ROWS * BN / 4; g += gridDim.x * blockDim.x) {
-        const int row = g / (BN / 4);
-        const int col = (g - row * (BN / 4)) * 4;
-        if (t.m0 + row >= p.m || t.n0 + col >= p.n) continue;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int w = w0; w <= w1; ++w) {
-            const long long first_rel = (iters * w / workers) / kb;
-            const int slot = r == first_rel ? 2 * w : 2 * w + 1;
-            const float4 v = *reinterpret_cast<const float4*>(
-                p.partials + static_cast<long long>(slot) * (ROWS * BN) + static_cast<long long>(row) * BN + col);
-            if (w == w0) {
-                acc = v;
-            } else {
-                acc.x += v.x;
-                acc.y += v.y;
-                acc.z += v.z;
-                acc.w += v.w;
-            }
+    const int rows = min(ROWS, p.m - t.m0);
+    const int cols = min(BN, p.n - t.n0);
+    constexpr size_t kSlot = static_cast<size_t>(ROWS) * BN;
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < ROWS * kGroupsPerRow; g += gridDim.x * blockDim.x) {
+        const int row = g / kGroupsPerRow;
+        const int col = (g % kGroupsPerRow) * 4;
+        if (row >= rows || col >= cols) continue;
+        const size_t off = static_cast<size_t>(row) * BN + col;
+        float4 acc = *reinterpret_cast<const float4*>(p.partials + first_slot * kSlot + off);
+        for (int w = w0 + 1; w <= w1; ++w) {
+            const float4 v = *reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(2 * w) * kSlot + off);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
         }
         const float out[4] = {acc.x, acc.y, acc.z, acc.w};
         Store::template store<4>(p, st, row, col, out);
@@ -396,16 +405,23 @@ mfb_status_t worker_count(const TcEntry* e, int dev, int sm_limit, int* out) {
 }
 
 // Stream-K share of a launch: how many of the last tiles split their K blocks among all
-// workers (0: every tile data parallel). Whole tiles are dealt out while that keeps at least
-// 90% of the workers busy in the last wave; otherwise the last one or two waves' worth of
-// tiles (all tiles when there is less than one wave) are shared, provided every worker
-// still gets at least kMinSkBlocks K blocks (shorter shares would spend more on filling the
-// pipeline and on the fix-up than they save). The reference's GemmPlan leaves this to
-// cuBLASLt's heuristic (src/ops/gemm/plan/implementation.inc:13-60).
+// workers (0: every tile data parallel). The reference's GemmPlan leaves this choice to
+// cuBLASLt's heuristic (src/ops/gemm/plan/implementation.inc:13-60). Measured on B200
+// (strict FP32, GEMM phase):
+//  * one wave or more whose last wave leaves more than a tenth of the workers idle: the last
+//    one or two waves' worth of tiles are shared (4096^3: 554 us against 678 us whole);
+//  * tiles for at most 60% of the workers: all tiles are shared (512 x 512 x 65536: 180 us
+//    against 1196-2193 us whole);
+//  * tiles for 60-100% of the workers stay whole: 2048^3 took 87.7 us whole and 100.9 us
+//    shared. Workers at staggered K offsets lose the L2 reuse that tiles moving through K in
+//    lockstep get, and the fix-up pass costs more than the idle tenth of the SMs;
+//  * every worker needs at least kMinSkBlocks K blocks: shorter shares spend more on filling
+//    the pipeline and on the fix-up than they save.
 constexpr int kMinSkBlocks = 8;
 
 long long streamk_tiles(long long tiles, int workers, int kb) {
     if (workers <= 1 || tiles <= 0 || kb <= 0) return 0;
+    if (tiles < workers && tiles * 10 > static_cast<long long>(workers) * 6) return 0;
     const long long waves = (tiles + workers - 1) / workers;
     if (tiles * 10 >= waves * workers * 9) return 0;
     const long long full = tiles / workers;
@@ -447,7 +463,8 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch)
     // Estimated rate of each admissible kernel, as or without a stream-K launch: the tile
     // shape's per-SM rate (measured order: SM-pair 256 x 256 tiles, which halve B's
     // shared-memory traffic per FLOP, then 128 x 256, 128 x 128, 128 x 64) times the share of
-    // workers that stay busy (whole waves of tiles, or ~95% with a stream-K share).
+    // workers that stay busy (whole waves of tiles, or ~90% with a stream-K share, the
+    // fix-up included). mfb_plan_tune measures every candidate instead.
     struct Scored {
         TcConfig c;
         double score;
@@ -473,7 +490,7 @@ int tc_candidates(const mfb_gemm_desc& d, TcConfig* out, int max_out, int batch)
         all[n_all++] = Scored{c, rate * busy};
         if (streamk_tiles(tiles, workers, kb_count(d, e)) > 0) {
             c.stream_k = 1;
-            all[n_all++] = Scored{c, rate * std::max(busy, 0.95)};
+            all[n_all++] = Scored{c, rate * std::max(busy, 0.9)};
         }
     }
     std::stable_sort(all, all + n_all, [](const Scored& x, const Scored& y) { return x.score > y.score; });
@@ -709,8 +726,8 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     int w = static_cast<int>(sc.workers);
     void* rargs[] = {&p, &w};
     cudaLaunchConfig_t rc{};
-    const int per_tile = tile_rows * cfg.bn / 4;
-    rc.gridDim = dim3(static_cast<unsigned>((per_tile + 255) / 256), static_cast<unsigned>(p.sk_tiles));
+    const int per_tile = tile_rows * cfg.bn / 4;  // float4 groups of one tile, 4 per thread
+    rc.gridDim = dim3(static_cast<unsigned>((per_tile + 1023) / 1024), static_cast<unsigned>(p.sk_tiles));
     rc.blockDim = dim3(256);
     rc.stream = stream;
     rc.attrs = &pdl;

@@ -9,6 +9,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <vector>
 
 namespace mfb {
 
@@ -153,6 +154,15 @@ mfb_status_t conv2d_bwd_bias_launch(int device, cudaStream_t stream, int n, int 
 mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h, int w, int k, int r, int s,
                            int stride, int pad, const float* x, const float* wgt, const float* bias, float* y,
                            int precision);
+
+// ---------------------------------------------------------------------- NCCL (collectives.cu)
+// The cached communicator set (ncclCommInitAll) of a list of distinct devices of this process:
+// its per-device non-blocking streams, in device-list order.
+mfb_status_t nccl_streams(const std::vector<int>& devices, std::vector<cudaStream_t>* streams);
+// In-place ncclBroadcast of `count` floats from bufs[root] into every bufs[r] (on devices[r]), one
+// NCCL group, enqueued on the set's streams; returns without waiting.
+mfb_status_t nccl_broadcast_group(const std::vector<int>& devices, const std::vector<float*>& bufs, size_t count,
+                                  int root);
 
 // ---------------------------------------------------------------------- naive
 mfb_status_t naive_launch(const mfb_gemm_desc& d, cudaStream_t stream, const float* a, const float* b, float* c,

@@ -306,6 +306,13 @@ def test_prepare_operands_one_at_a_time(precision):
     B = torch.randn((k, n), device="cuda", generator=g)
     C0 = torch.randn((m, n), device="cuda", generator=g)
     p = mf.GemmPlan(m, n, k, mf.GemmOptions(precision=precision))
+    # Column ranges run whole tiles; compare with the plan's first candidate that does too
+    # (a stream-K launch adds the K shares in another order).
+    for i in range(p.candidate_count()):
+        p.select_candidate(i)
+        if p.info().stream_k_tiles == 0:
+            break
+    assert p.info().stream_k_tiles == 0
     want = C0.clone()
     p.execute(A, B, want, 0.5, 1.0)
     got = C0.clone()
@@ -342,6 +349,13 @@ def test_column_range_phases_equal_execute(precision):
     B = torch.randn((k, n), device="cuda", generator=g)
     C0 = torch.randn((m, n), device="cuda", generator=g)
     p = mf.GemmPlan(m, n, k, mf.GemmOptions(precision=precision))
+    # Column ranges run whole tiles; compare with the plan's first candidate that does too
+    # (a stream-K launch adds the K shares in another order).
+    for i in range(p.candidate_count()):
+        p.select_candidate(i)
+        if p.info().stream_k_tiles == 0:
+            break
+    assert p.info().stream_k_tiles == 0
     want = C0.clone()
     p.execute(A, B, want, 0.5, 1.0)
     lib, h, s = _lib.lib(), p._handle, _stream_handle()

@@ -40,6 +40,8 @@ def streamk_tiles(tiles, workers, kb, min_blocks=8):
     """The host policy of gemm_tc.cu (streamk_tiles)."""
     if workers <= 1 or tiles <= 0 or kb <= 0:
         return 0
+    if tiles < workers and tiles * 10 > workers * 6:
+        return 0
     waves = -(-tiles // workers)
     if tiles * 10 >= waves * workers * 9:
         return 0
@@ -102,8 +104,12 @@ def test_every_k_block_once_and_slots_distinct(tiles, workers, kb):
 
 
 def test_policy_picks_shapes_that_leave_workers_idle():
-    # 2048^3 on 74 SM pairs: 64 tiles of 256 x 256, 64 K blocks each -> all shared.
-    assert streamk_tiles(64, 74, 64) == 64
+    # 2048^3 on 74 SM pairs: 64 tiles of 256 x 256 fill 86% of the pairs -> whole tiles
+    # (measured faster than sharing); on 148 SMs with 128 x 128 tiles (1.73 waves) -> shared
+    assert streamk_tiles(64, 74, 64) == 0
+    assert streamk_tiles(256, 148, 64) == 256
+    # 4096^3 on pairs: 256 tiles, 3.46 waves -> the last 1.46 waves' worth shared
+    assert streamk_tiles(256, 74, 128) == 256 - 2 * 74
     # the linear layer 8192 x 11008 on pairs: 1376 tiles, 18.6 waves -> data parallel
     assert streamk_tiles(1376, 74, 128) == 0
     # 1.2 waves: the last ~1.2 waves are shared, earlier waves stay whole
