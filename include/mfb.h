@@ -141,6 +141,28 @@ MFB_API mfb_status_t mfb_sgemm(int device, mfb_stream_t stream, const mfb_gemm_d
 MFB_API mfb_status_t mfb_sgemm_host(int device, mfb_stream_t stream, const mfb_gemm_desc* desc, const float* a,
                                     const float* b, float* c, const float* bias);
 
+/* ---------------------------------------------------------------- row-split GEMM over GPUs */
+/* One block of rows of A and C on one GPU of this process. */
+typedef struct mfb_row_block {
+    int device;      /* CUDA device holding the block (one block per device) */
+    int rows;        /* rows of A and C in the block (>= 0); the blocks' rows add up to desc->m */
+    const float* a;  /* rows x k of A, row stride desc->lda, memory of `device` */
+    float* c;        /* rows x n of C, row stride desc->ldc, memory of `device` */
+} mfb_row_block;
+
+/* C = epilogue(alpha * A * B + beta * C) over several GPUs: block r holds rows of A and C on
+ * blocks[r].device (blocks in row order), B (k x n, row stride desc->ldb) and the bias (n
+ * floats, iff epilogue != NONE) are memory of blocks[root].device. B and the bias reach the
+ * other GPUs by NCCL broadcasts over NVLink/NVSwitch, B in column panels, and every GPU
+ * multiplies the panels that have arrived while later ones are in flight; C stays split.
+ * trans_a/trans_b must be 0; precision as mfb_sgemm. Blocking: work already queued on the
+ * devices finishes first, and the call returns when every GPU is done. Calls are serialized.
+ * The multi-GPU form of the GPU share of HeterogeneousScheduler::gemm (src/hw/scheduler.cpp:
+ * 238-312: a block of rows on one device, B sent over PCIe) and of the host-staged broadcast
+ * (src/hw/collectives.cpp:219-235). */
+MFB_API mfb_status_t mfb_sgemm_multi(const mfb_row_block* blocks, int block_count, int root,
+                                     const mfb_gemm_desc* desc, const float* b, const float* bias);
+
 /* ---------------------------------------------------------------- strided-batched GEMM */
 /* batch_count GEMMs that share one descriptor: C_i = epilogue(alpha op(A_i) op(B_i) + beta C_i)
  * with A_i = a + i*stride_a, B_i = b + i*stride_b, C_i = c + i*stride_c (strides in floats;

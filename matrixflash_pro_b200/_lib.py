@@ -19,7 +19,7 @@ MFB_OK, MFB_EINVAL, MFB_ECUDA, MFB_ETIMEOUT, MFB_ENCCL, MFB_EUNSUPPORTED, MFB_EN
 EXPORTED_SYMBOLS = (
     "mfb_status_string", "mfb_last_error", "mfb_version", "mfb_device_status", "mfb_set_wait_limit_ns",
     "mfb_get_wait_limit_ns", "mfb_sync", "mfb_cuda_gemm", "mfb_cuda_sync", "mfb_cuda_device_count", "mfb_sgemm", "mfb_sgemm_host",
-    "mfb_sgemm_noalloc", "mfb_sgemm_strided_batched",
+    "mfb_sgemm_multi", "mfb_sgemm_noalloc", "mfb_sgemm_strided_batched",
     "mfb_plan_create", "mfb_plan_execute", "mfb_plan_prepare", "mfb_plan_multiply", "mfb_plan_prepare_cols",
     "mfb_plan_multiply_cols", "mfb_plan_set_sm_limit",
     "mfb_plan_tune", "mfb_plan_select_candidate", "mfb_plan_info_get", "mfb_plan_destroy", "mfb_gemv",
@@ -41,6 +41,11 @@ class GemmDesc(ctypes.Structure):
 class CollectiveBuffer(ctypes.Structure):
     """mfb_collective_buffer (include/mfb.h)."""
     _fields_ = [("data", ctypes.c_void_p), ("count", ctypes.c_size_t), ("device", ctypes.c_int)]
+
+
+class RowBlock(ctypes.Structure):
+    """mfb_row_block (include/mfb.h)."""
+    _fields_ = [("device", ctypes.c_int), ("rows", ctypes.c_int), ("a", ctypes.c_void_p), ("c", ctypes.c_void_p)]
 
 
 class PlanInfo(ctypes.Structure):
@@ -75,6 +80,8 @@ def _declare(lib):
         "mfb_sgemm": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_sgemm_host": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
         "mfb_sgemm_noalloc": (st, [ctypes.c_int, _vp, ctypes.POINTER(GemmDesc), _vp, _vp, _vp, _vp]),
+        "mfb_sgemm_multi": (st, [ctypes.POINTER(RowBlock), ctypes.c_int, ctypes.c_int, ctypes.POINTER(GemmDesc), _vp,
+                                 _vp]),
         "mfb_all_reduce": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int, ctypes.c_int]),
         "mfb_broadcast": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_int]),
         "mfb_all_gather": (st, [ctypes.POINTER(CollectiveBuffer), ctypes.c_int, ctypes.c_size_t]),

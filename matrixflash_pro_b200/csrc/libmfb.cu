@@ -9,4 +9,5 @@
 #include "peak_probe.cu"
 #include "collectives.cu"
 #include "host_gemm.cu"
+#include "multi_gemm.cu"
 #include "plugin.cu"

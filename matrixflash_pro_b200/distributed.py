@@ -30,6 +30,33 @@ from .errors import InvalidArgumentError
 from .gemm import GemmPrecision, _stream_handle, make_desc
 
 
+def sgemm_multi(a_blocks: List[torch.Tensor], b: torch.Tensor, c_blocks: List[torch.Tensor], alpha: float = 1.0,
+                beta: float = 0.0, precision: GemmPrecision = GemmPrecision.fp32, root: int = 0,
+                bias: Optional[torch.Tensor] = None, epilogue: int = 0) -> None:
+    """The row split inside one process (mfb_sgemm_multi): block r of A (rows_r x k) and of C
+    (rows_r x n) on its own GPU, B (k x n) and the bias on block `root`'s GPU; B reaches the other
+    GPUs by NCCL broadcasts in column panels. Blocking. Row strides come from the tensors (padded
+    rows allowed); all blocks share lda and ldc."""
+    if len(a_blocks) != len(c_blocks) or not a_blocks:
+        raise InvalidArgumentError("one A block and one C block per GPU")
+    from .gemm import _ld
+    k, n = int(b.shape[0]), int(b.shape[1])
+    lda = max(_ld(t, "A") for t in a_blocks) if k else 1
+    ldc = max(_ld(t, "C") for t in c_blocks)
+    blocks = (_lib.RowBlock * len(a_blocks))()
+    m = 0
+    for i, (a, c) in enumerate(zip(a_blocks, c_blocks)):
+        if int(a.shape[0]) != int(c.shape[0]) or int(c.shape[1]) != n or int(a.shape[1]) != k:
+            raise InvalidArgumentError("A and C blocks must have matching rows, k and n")
+        if int(c.shape[0]) > 1 and ((k and _ld(a, "A") != lda) or _ld(c, "C") != ldc):
+            raise InvalidArgumentError("all A blocks share one row stride, and all C blocks another")
+        blocks[i] = _lib.RowBlock(c.device.index, int(c.shape[0]), a.data_ptr() if a.numel() else 0, c.data_ptr())
+        m += int(c.shape[0])
+    desc = make_desc(m, n, k, lda, _ld(b, "B") if k else max(1, n), ldc, alpha, beta, int(precision), 0, 0, epilogue)
+    _lib.check(_lib.lib().mfb_sgemm_multi(blocks, len(a_blocks), int(root), ctypes.byref(desc), b.data_ptr(),
+                                          bias.data_ptr() if bias is not None else 0), "sgemm_multi")
+
+
 def row_partition(m: int, world: int, rank: int) -> Tuple[int, int]:
     """Rows [begin, end) of rank `rank`: ceil(m / world) per rank, the last rank takes the rest."""
     if world < 1 or not 0 <= rank < world:
