@@ -66,19 +66,34 @@ def row_partition(m: int, world: int, rank: int) -> Tuple[int, int]:
     return begin, min(m, begin + per)
 
 
-def col_panels(n: int, world: int, first_fraction: float = 0.1, tile: int = 256) -> List[Tuple[int, int]]:
-    """Column panels for the broadcast/GEMM pipeline: one small leading panel of whole
-    256-column tiles (its broadcast is the only exposed transfer) and one panel for the rest.
-    A single panel without peers. Measured on 2 B200s with the linear layer (n = 11008): a
-    1024-column first panel whose GEMM leaves 32 SMs to NCCL gave the shortest step; 512 and
-    2048 columns, 16 SMs, or no split at all were slower (NCCL's broadcast occupies more than
-    16 SMs, so a grid of 132 SMs no longer fits beside it and needs an extra wave)."""
+def col_panels(n: int, world: int, k: int = 0, first_fraction: float = 0.1, tile: int = 256,
+               max_first_bytes: int = 128 << 20, stop_ratio: int = 4) -> List[Tuple[int, int]]:
+    """Column panels for the broadcast/GEMM pipeline. A single panel without peers.
+
+    The first panel's broadcast is the only transfer nothing hides, so it is small: a tenth of
+    the columns in whole 256-column tiles (measured best on 2 B200s for the linear layer,
+    n = 11008: 1024 columns), and at most max_first_bytes of B. Each later panel must arrive
+    while the GEMM of the one before runs; a panel's GEMM takes 2 * m_local * k FLOP per
+    column and its transfer 4 * k bytes per column, so with m_local in the thousands a panel
+    twice as wide as the previous one arrives in time. Panels therefore double until the
+    rest of B is at most stop_ratio times the last panel, and the rest is the final panel.
+    For n = 32768, k = 32768 (a 4.3 GB B): 1024, 2048, 4096, 8192, 17408 columns, where two
+    panels (3072 + 29696) would leave the GPUs waiting for the 3.9 GB second one."""
     if world <= 1 or n <= 2 * tile:
         return [(0, n)]
     first = max(tile, int(n * first_fraction) // tile * tile)
+    if k > 0:
+        first = min(first, max(tile, max_first_bytes // (4 * k) // tile * tile))
     if first >= n:
         return [(0, n)]
-    return [(0, first), (first, n)]
+    panels = [(0, first)]
+    width, start = first, first
+    while n - start > stop_ratio * width:
+        width *= 2
+        panels.append((start, start + width))
+        start += width
+    panels.append((start, n))
+    return panels
 
 
 @dataclass
@@ -88,8 +103,8 @@ class PanelSchedule:
     sm_limits: List[Optional[int]]
 
 
-def schedule(n: int, world: int, comm_sms: int, total_sms: int) -> PanelSchedule:
-    panels = col_panels(n, world)
+def schedule(n: int, world: int, comm_sms: int, total_sms: int, k: int = 0) -> PanelSchedule:
+    panels = col_panels(n, world, k)
     # While later panels are still broadcasting, leave comm_sms SMs to NCCL.
     limits = [max(1, total_sms - comm_sms) if i < len(panels) - 1 else None for i in range(len(panels))]
     return PanelSchedule(panels, limits)
@@ -218,7 +233,7 @@ class RowSplitGemm:
         total_sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.plan = _PointerPlan(self.device, m_local, n, k, lda, ldb, ldc, int(precision))
         self.plans = [self.plan]
-        self.sched = schedule(n, self.world if self.plan.tcgen05 else 1, comm_sms, total_sms)
+        self.sched = schedule(n, self.world if self.plan.tcgen05 else 1, comm_sms, total_sms, k)
         # Contiguous column panels of B, the broadcast buffers (several ranks only).
         self.panel_bufs: List[torch.Tensor] = []
         self.side = torch.cuda.Stream(self.device) if self.world > 1 else None
