@@ -55,6 +55,30 @@ constexpr int kPackMaxWp = 512;  // padded width the shared tile holds; wider im
 size_t pack_rows_smem_bytes(int w) { return static_cast<size_t>(kPackRows) * w * kPackStride * 4; }
 
 __global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __restrict__ x, int c, int h, int w,
+                                                             int pad_h, int pad_w, int cp, int hp, int wp, int vec,
+                                                             float* __restrict__ hi, float* __restrict__ lo);
+
+// The pack kernel's shared tile grows with the image width (up to kPackMaxWp): its dynamic
+// shared-memory limit is raised to the largest tile once per device, under a lock, so host
+// threads packing images of different widths never race on the attribute.
+mfb_status_t allow_pack_rows_smem() {
+    static std::mutex mutex;
+    static std::vector<char> done;
+    int dev = 0;
+    MFB_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(mutex);
+    if (static_cast<int>(done.size()) <= dev) done.resize(dev + 1, 0);
+    if (!done[dev]) {
+        MFB_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(&conv_pack_rows_kernel),
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(pack_rows_smem_bytes(kPackMaxWp))),
+                     "conv prepass smem attribute");
+        done[dev] = 1;
+    }
+    return MFB_OK;
+}
+
+__global__ void __launch_bounds__(256) conv_pack_rows_kernel(const float* __restrict__ x, int c, int h, int w,
                                                              int pad_h, int pad_w, int cp, int hp, int wp, int vec2,
                                                              float* __restrict__ hi, float* __restrict__ lo) {
     extern __shared__ float tile[];  // [kPackRows][w][kPackStride]
@@ -499,11 +523,7 @@ mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g,
     float* b_lo = planes == 2 ? b_hi + b_plane : nullptr;
     if (wp <= kPackMaxWp) {
         const size_t tile_bytes = pack_rows_smem_bytes(w);
-        if (tile_bytes > 48 * 1024)
-            MFB_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(&conv_pack_rows_kernel),
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(tile_bytes)),
-                         "conv prepass smem attribute");
+        MFB_TRY(allow_pack_rows_smem());
         const int vec = (w % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) ? 1 : 0;
         dim3 pgrid(static_cast<unsigned>((hp + kPackRows - 1) / kPackRows), static_cast<unsigned>((cp + 31) / 32), n);
         conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, g.pad_h, g.pad_w, cp, hp, wp, vec,
@@ -687,11 +707,7 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     // X planes (as the forward), dY planes in X's padded width.
     if (wp <= kPackMaxWp) {
         const size_t tile_bytes = pack_rows_smem_bytes(w);
-        if (tile_bytes > 48 * 1024)
-            MFB_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(&conv_pack_rows_kernel),
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(tile_bytes)),
-                         "conv prepass smem attribute");
+        MFB_TRY(allow_pack_rows_smem());
         const int vec = (w % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) ? 1 : 0;
         dim3 pgrid(static_cast<unsigned>((hp + kPackRows - 1) / kPackRows), static_cast<unsigned>((cp + 31) / 32), n);
         conv_pack_rows_kernel<<<pgrid, 256, tile_bytes, stream>>>(x, c, h, w, pad, pad, cp, hp, wp, vec, a_hi, a_lo);
