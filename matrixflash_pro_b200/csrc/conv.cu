@@ -10,6 +10,8 @@
 #include "mfb_internal.h"
 
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 #include <mutex>
 
 namespace mfb {
@@ -17,7 +19,35 @@ namespace mfb {
 namespace {
 
 constexpr int kConvThreads = 256;
-constexpr double kConvDirectMaxFlops = 1e7;  // below this the direct kernel beats the tcgen05 path
+// Stride-1 convs below these sizes run the direct kernel (measured with CUDA-graph replay on
+// B200, 32 x 32 images, 3 x 3 filters): the tensor path pays three launches and a pipeline
+// fill (~12 us), and pads channels to 32-channel slabs, so with C <= 4 it does 8x or more
+// of useless K work. C = 3, K = 16: 8 images 6.4 us direct vs 15.3 us tcgen05, 64 images
+// 28.6 vs 52.3 us (57 MFLOP); 8 x 3 x 64 x 64 with 64 filters (113 MFLOP): 54.2 vs 43.6 us.
+// C = 8 at 19 MFLOP: 14.1 vs 13.4 us; C >= 16 at 19 MFLOP and above: the tensor path wins.
+constexpr double kConvDirectMaxFlops = 1e7;
+constexpr double kConvDirectMaxFlopsNarrowC = 8e7;  // C <= 4
+constexpr int kConvNarrowC = 4;
+
+// Algorithm override for measurements: MFB_CONV_ALGO = direct | implicit_gemm (anything
+// else, or unset: the size rule above). implicit_gemm applies to stride 1 only; other
+// strides always run the direct kernel. Read once per process.
+int conv_algo_override() {
+    static const int algo = [] {
+        const char* v = std::getenv("MFB_CONV_ALGO");
+        if (!v) return 0;
+        const std::string s(v);
+        return s == "direct" ? 1 : s == "implicit_gemm" ? 2 : 0;
+    }();
+    return algo;
+}
+
+bool conv_use_direct(int stride, double flops, int c) {
+    if (stride != 1) return true;
+    const int algo = conv_algo_override();
+    if (algo != 0) return algo == 1;
+    return flops < (c <= kConvNarrowC ? kConvDirectMaxFlopsNarrowC : kConvDirectMaxFlops);
+}
 
 __device__ __forceinline__ float conv_round_tf32(float x) {
     uint32_t r;
@@ -606,12 +636,11 @@ mfb_status_t conv2d_launch(int device, cudaStream_t stream, int n, int c, int h,
     const int P = (h + 2 * pad - r) / stride + 1;
     const int Q = (w + 2 * pad - s) / stride + 1;
     if (n == 0 || P <= 0 || Q <= 0) return MFB_OK;
-    // Other strides, and problems too small to amortize the tensor path's three launches and
-    // pipeline fill (~25 us; e.g. 8x3x32x32 with 16 filters, 7 MFLOP): the direct kernel,
-    // one launch, FP32 FMA chains in the reference's order (at least as accurate as either
-    // precision policy asks).
+    // Other strides, and problems too small to amortize the tensor path (conv_use_direct):
+    // the direct kernel, one launch, FP32 FMA chains in the reference's order (at least as
+    // accurate as either precision policy asks).
     const double flops = 2.0 * n * k * P * Q * static_cast<double>(c) * r * s;
-    if (stride != 1 || flops < kConvDirectMaxFlops)
+    if (conv_use_direct(stride, flops, c))
         return conv2d_direct(stream, n, c, h, w, k, r, s, stride, pad, P, Q, x, wgt, bias, y);
     return conv_tc_forward(device, stream, ConvGeom{n, c, h, w, k, r, s, pad, pad}, x, wgt, 0, bias, y, precision);
 }

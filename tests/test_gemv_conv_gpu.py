@@ -149,6 +149,8 @@ def test_conv_known_answers():
 
 @pytest.mark.parametrize("n,c,h,w,k,r,s,stride,pad", [
     (2, 64, 56, 56, 64, 3, 3, 1, 1), (3, 7, 13, 11, 5, 3, 3, 1, 1), (1, 16, 20, 24, 32, 5, 5, 2, 2),
+    # 3 channels, 28 MFLOP: the direct kernel (narrow-channel rule), past the plain FLOP cutoff
+    (32, 3, 32, 32, 16, 3, 3, 1, 1),
     (2, 3, 9, 9, 4, 1, 1, 1, 0), (1, 33, 17, 15, 48, 3, 1, 1, 1),
     # wide rows (a 128-position tile spans less than two padded rows); 200 filters: one
     # 256-wide filter tile (no stacked B); 160 filters: BN = 256 as well
