@@ -584,7 +584,7 @@ def run_aux_workload(args):
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with torch.cuda.graph(graph, stream=side):  # the stream whose library scratch exists
             for _ in range(args.steps):
                 step()
         graph.replay()  # warm replay
