@@ -115,7 +115,7 @@ __global__ void scale_epilogue_kernel(float* __restrict__ c, long long ldc, int 
 // TcWorkIter) is the sum of its partial slots, added in K order (worker order), then
 // written through the GEMM's own store (alpha, beta * C, bias, activation). Tiles that one
 // worker covered whole were written by the GEMM and are skipped. blockIdx.y = stream-K
-// tile; the x blocks split its ROWS x BN values, four consecutive columns per thread step.
+// tile; the x blocks split its ROWS x BN values, four consecutive columns per thread.
 // Workers w0 < w <= w1 of a shared tile r start their ranges inside it, so they hold it in
 // slot 2w; only w0 may have started in an earlier tile (slot 2 w0 + 1). Thread 0 finds
 // w0, w1 and that first slot once per block.
@@ -149,14 +149,26 @@ __global__ void __launch_bounds__(256) streamk_reduce_kernel(const GemmTcParams 
         const int col = (g % kGroupsPerRow) * 4;
         if (row >= rows || col >= cols) continue;
         const size_t off = static_cast<size_t>(row) * BN + col;
+        auto slot_at = [&](int w) {
+            return *reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(2 * w) * kSlot + off);
+        };
+        auto add = [](float4& a, const float4& v) {
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
+        };
         float4 acc = *reinterpret_cast<const float4*>(p.partials + first_slot * kSlot + off);
-        for (int w = w0 + 1; w <= w1; ++w) {
-            const float4 v = *reinterpret_cast<const float4*>(p.partials + static_cast<size_t>(2 * w) * kSlot + off);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+        int w = w0 + 1;
+        // Four shares' loads in flight at a time; the adds stay in K order.
+        for (; w + 3 <= w1; w += 4) {
+            const float4 v0 = slot_at(w), v1 = slot_at(w + 1), v2 = slot_at(w + 2), v3 = slot_at(w + 3);
+            add(acc, v0);
+            add(acc, v1);
+            add(acc, v2);
+            add(acc, v3);
         }
+        for (; w <= w1; ++w) add(acc, slot_at(w));
         const float out[4] = {acc.x, acc.y, acc.z, acc.w};
         Store::template store<4>(p, st, row, col, out);
     }
@@ -726,8 +738,8 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
     int w = static_cast<int>(sc.workers);
     void* rargs[] = {&p, &w};
     cudaLaunchConfig_t rc{};
-    const int per_tile = tile_rows * cfg.bn / 4;  // float4 groups of one tile, 4 per thread
-    rc.gridDim = dim3(static_cast<unsigned>((per_tile + 1023) / 1024), static_cast<unsigned>(p.sk_tiles));
+    const int per_tile = tile_rows * cfg.bn / 4;  // float4 groups of one tile, one per thread
+    rc.gridDim = dim3(static_cast<unsigned>((per_tile + 255) / 256), static_cast<unsigned>(p.sk_tiles));
     rc.blockDim = dim3(256);
     rc.stream = stream;
     rc.attrs = &pdl;
