@@ -131,7 +131,7 @@ __global__ void scale_kernel(float* __restrict__ p, size_t count, float factor) 
         p[i] *= factor;
 }
 
-int grid_for(size_t count) { return static_cast<int>(std::min<size_t>((count + 255) / 256, 148 * 8)); }
+int grid_for(size_t count) { return static_cast<int>(std::min<size_t>((count + 255) / 256, static_cast<size_t>(current_sm_count()) * 8)); }
 
 // ------------------------------------------------------------------------------ common checks
 struct Plan {

@@ -297,7 +297,7 @@ mfb_status_t conv2d_direct(cudaStream_t stream, int n, int c, int h, int w, int 
 // ------------------------------------------------------------------------------------ backward kernels
 
 // dy (N,K,P,Q) -> G [N][K][ldy]: output positions j = p*Wp + q of X's padded width, zeros for
-// q >= Q and j >= P*Wp. grid (ceil(ldy / 4 / 128), up to 16 x 148 row slots): a thread writes 4
+// q >= Q and j >= P*Wp. grid (ceil(ldy / 4 / 128), up to 16 row slots per SM): a thread writes 4
 // positions of every grid.y-th (image, filter) row; one multiply-shift division locates its first
 // position, the others follow by wrapping q (no per-element integer division: the kernel was
 // issue-bound).
@@ -564,7 +564,7 @@ mfb_status_t conv_tc_forward(int device, cudaStream_t stream, const ConvGeom& g,
     }
     MFB_CUDA_TRY(cudaGetLastError(), "conv input prepass launch");
     const long long wgroups = static_cast<long long>(r) * s * k * (cp / 4);
-    conv_pack_weights_kernel<<<static_cast<int>(std::min<long long>((wgroups + 255) / 256, 148LL * 4)), 256, 0,
+    conv_pack_weights_kernel<<<static_cast<int>(std::min<long long>((wgroups + 255) / 256, static_cast<long long>(current_sm_count()) * 4)), 256, 0,
                                stream>>>(wgt, k, c, r, s, cp, flip, b_hi, b_lo);
     MFB_CUDA_TRY(cudaGetLastError(), "conv weight prepass launch");
 
@@ -658,7 +658,7 @@ mfb_status_t conv2d_bwd_data_launch(int device, cudaStream_t stream, int n, int 
         return conv_tc_forward(device, stream, ConvGeom{n, k, P, Q, c, r, s, r - 1 - pad, s - 1 - pad}, dy, wgt, 1,
                                nullptr, dx, precision);
     const long long total = static_cast<long long>(n) * c * h * w;
-    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, static_cast<long long>(current_sm_count()) * 16));
     conv_bwd_data_direct_kernel<<<blocks, 256, 0, stream>>>(dy, wgt, dx, n, c, h, w, k, r, s, P, Q, stride, pad);
     MFB_CUDA_TRY(cudaGetLastError(), "conv2d input-gradient launch");
     return MFB_OK;
@@ -685,7 +685,7 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     const bool tensor = stride == 1 && flops >= kConvDirectMaxFlops && e != nullptr && n <= 65535 &&
                         npos <= 0x7fffffffLL && gpos <= 0x7fffffffLL && n * ((gpos + 31) / 32) < (1LL << 30);
     if (!tensor) {
-        const int blocks = static_cast<int>(std::min<long long>((wtotal + 127) / 128, 148LL * 16));
+        const int blocks = static_cast<int>(std::min<long long>((wtotal + 127) / 128, static_cast<long long>(current_sm_count()) * 16));
         conv_bwd_filter_direct_kernel<<<blocks, 128, 0, stream>>>(dy, x, dw, n, c, h, w, k, r, s, P, Q, stride, pad);
         MFB_CUDA_TRY(cudaGetLastError(), "conv2d weight-gradient launch");
         return MFB_OK;
@@ -746,7 +746,7 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     }
     MFB_CUDA_TRY(cudaGetLastError(), "wgrad input prepass launch");
     const long long grad_rows = static_cast<long long>(n) * k;
-    dim3 ggrid(static_cast<unsigned>((ldy / 4 + 127) / 128), static_cast<unsigned>(std::min(grad_rows, 148LL * 16)));
+    dim3 ggrid(static_cast<unsigned>((ldy / 4 + 127) / 128), static_cast<unsigned>(std::min(grad_rows, static_cast<long long>(current_sm_count()) * 16)));
     conv_pack_grad_kernel<<<ggrid, 128, 0, stream>>>(dy, P, Q, wp, ldy, grad_rows,
                                                      make_fastdiv(static_cast<uint32_t>(wp)), g_hi, g_lo);
     MFB_CUDA_TRY(cudaGetLastError(), "wgrad gradient prepass launch");
@@ -781,7 +781,7 @@ mfb_status_t conv2d_bwd_filter_launch(int device, cudaStream_t stream, int n, in
     const int grid = static_cast<int>(std::min<long long>(tiles, sms));
     MFB_CUDA_TRY(cudaLaunchKernel(e->fn, dim3(grid), dim3(e->threads), args, static_cast<size_t>(e->smem), stream),
                  "tcgen05 weight-gradient launch");
-    const int rblocks = static_cast<int>(std::min<long long>((wtotal + 255) / 256, 148LL * 8));
+    const int rblocks = static_cast<int>(std::min<long long>((wtotal + 255) / 256, static_cast<long long>(current_sm_count()) * 8));
     conv_wgrad_reduce_kernel<<<rblocks, 256, 0, stream>>>(p.partial, p.splits, rows_alloc, p.ld_partial, k, c, r * s,
                                                           cg, dw);
     MFB_CUDA_TRY(cudaGetLastError(), "wgrad reduce launch");
@@ -818,7 +818,7 @@ mfb_status_t conv2d_bwd_bias_launch(int device, cudaStream_t stream, int n, int 
     float* ones = static_cast<float*>(ws);
     float* sums = ones + ones_bytes / 4;
     void* gemv_ws = gemv_bytes ? static_cast<void*>(sums + sums_bytes / 4) : nullptr;
-    conv_fill_kernel<<<static_cast<int>(std::min<long long>((plane + 255) / 256, 148LL * 4)), 256, 0, stream>>>(
+    conv_fill_kernel<<<static_cast<int>(std::min<long long>((plane + 255) / 256, static_cast<long long>(current_sm_count()) * 4)), 256, 0, stream>>>(
         ones, plane, 1.0f);
     MFB_CUDA_TRY(cudaGetLastError(), "dB ones launch");
     MFB_TRY(gemv_launch(d, stream, dy, ones, sums, nullptr, gemv_ws, gemv_bytes));

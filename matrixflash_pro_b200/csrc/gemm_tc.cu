@@ -560,7 +560,7 @@ size_t tc_workspace_bytes(const mfb_gemm_desc& d, int batch) {
 mfb_status_t scale_output(const mfb_gemm_desc& d, cudaStream_t stream, float* c, const float* bias) {
     const long long total = static_cast<long long>(d.m) * d.n;
     if (total == 0) return MFB_OK;
-    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, static_cast<long long>(current_sm_count()) * 16));
     scale_epilogue_kernel<<<blocks, 256, 0, stream>>>(c, d.ldc, d.m, d.n, d.beta, bias, d.epilogue);
     MFB_CUDA_TRY(cudaGetLastError(), "scale/epilogue launch");
     return MFB_OK;
@@ -621,7 +621,7 @@ mfb_status_t tc_gemm(const mfb_gemm_desc& d, const TcConfig& cfg, cudaStream_t s
         used += need;
         const long long total_groups = static_cast<long long>(op.rows) * (ldp / 4);
         const int blocks = static_cast<int>(
-            std::min<long long>((total_groups + 255) / 256, std::max(1LL, 148LL * 8 / nb)));
+            std::min<long long>((total_groups + 255) / 256, std::max(1LL, static_cast<long long>(current_sm_count()) * 8 / nb)));
         if (which == 1 && cols.b_src != nullptr) {
             // columns [n0, n1) of B from a separate matrix, into the same columns of the planes
             const bool vec_c = cols.b_ld % 4 == 0 && aligned16(cols.b_src);

@@ -395,7 +395,7 @@ __global__ void gemv_cols_finish_kernel(const float* __restrict__ partial, int s
 // x^T for m == 1 lives in A's single row (lda irrelevant); it must be contiguous.
 int cols_splits(int n, int k) {
     const int col_blocks = (n + 511) / 512;
-    int splits = std::max(1, (148 * 8) / std::max(1, col_blocks));  // ~8 blocks of 4 warps per SM
+    int splits = std::max(1, (current_sm_count() * 8) / std::max(1, col_blocks));  // ~8 blocks of 4 warps per SM
     splits = std::min(splits, std::max(1, k / 32));
     return std::min(splits, 1024);
 }
@@ -405,7 +405,7 @@ void launch_rows(const mfb_gemm_desc& d, cudaStream_t stream, const float* a, co
                  const float* bias, int a_vec) {
     constexpr int kRowsPerBlock = (kGemvThreads / 32) * R;
     const long long row_blocks = (static_cast<long long>(d.m) + kRowsPerBlock - 1) / kRowsPerBlock;
-    const int grid = static_cast<int>(std::min<long long>(row_blocks, 148LL * 8));
+    const int grid = static_cast<int>(std::min<long long>(row_blocks, static_cast<long long>(current_sm_count()) * 8));
     gemv_rows_kernel<NC, R><<<grid, kGemvThreads, 0, stream>>>(a, d.lda, b, d.ldb, c, d.ldc, d.m, d.n, d.k,
                                                                d.alpha, d.beta, bias, d.epilogue, a_vec);
 }

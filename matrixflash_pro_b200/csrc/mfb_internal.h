@@ -45,6 +45,12 @@ private:
 // Makes `device` current after checking it exists and is an sm_100 part.
 mfb_status_t select_device(int device);
 int sm_count(int device);
+// SM count of the current device: the grid caps of the grid-stride kernels are multiples of it.
+inline int current_sm_count() {
+    int device = 0;
+    cudaGetDevice(&device);
+    return sm_count(device);
+}
 uint64_t wait_limit_ns();
 bool stream_capturing(cudaStream_t stream);
 

@@ -96,7 +96,7 @@ mfb_status_t covariance_run(int device, cudaStream_t stream, int rows, int cols,
     char* base = static_cast<char*>(ws);
     float* ones = reinterpret_cast<float*>(base + plan.ones_off);
     float* mean = reinterpret_cast<float*>(base + plan.mean_off);
-    const int fill_blocks = static_cast<int>(std::min<long long>((rows + 255) / 256, 148LL * 4));
+    const int fill_blocks = static_cast<int>(std::min<long long>((rows + 255) / 256, static_cast<long long>(current_sm_count()) * 4));
     fill_kernel<<<fill_blocks, 256, 0, stream>>>(ones, rows, 1.0f);
     MFB_CUDA_TRY(cudaGetLastError(), "covariance fill launch");
     MFB_TRY(gemv_launch(plan.mean_desc, stream, ones, x, mean, nullptr, base + plan.gemv_off, plan.gemv_bytes));
@@ -146,7 +146,7 @@ MFB_API mfb_status_t mfb_correlation(int device, mfb_stream_t stream_h, int rows
     float* cov = nullptr;
     MFB_TRY(mfb::covariance_run(device, stream, rows, cols, x, ldx, corr, ldcorr, precision, true, &cov));
     const long long total = static_cast<long long>(cols) * cols;
-    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 8));
+    const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, static_cast<long long>(current_sm_count()) * 8));
     mfb::cov_to_corr_kernel<<<blocks, 256, 0, stream>>>(cov, cols, corr, ldcorr, cols);
     MFB_CUDA_TRY(cudaGetLastError(), "correlation launch");
     return MFB_OK;
