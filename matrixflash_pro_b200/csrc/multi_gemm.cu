@@ -10,7 +10,8 @@
 // runs one process per GPU):
 //   * B travels in column panels: the root packs B[:, n0:n1] into a contiguous k x (n1 - n0)
 //     buffer and every panel is an NCCL broadcast on the set's communication streams; a small
-//     leading panel makes the first transfer, the only one not hidden, short.
+//     leading panel makes the first transfer, the only one not hidden, short, and for a large B
+//     the panels after it double in width so each arrives during the previous panel's GEMM.
 //   * Each GPU splits its A block into TF32 planes on its compute stream while B is in flight,
 //     splits each panel into the plan's B planes on a second stream as soon as it has arrived,
 //     and multiplies C[:, n0:n1] on the compute stream (mfb_plan_multiply_cols). GEMMs that
@@ -32,21 +33,33 @@ constexpr int kCommSms = 32;      // SMs left to NCCL while later panels are in 
 constexpr int kPanelTile = 256;   // panel widths are whole SM-pair tiles
 constexpr int kMaxBlocks = 64;
 
-// Column panels of B: one leading panel of about a tenth of the columns (whole 256-column
-// tiles), then the rest; a single panel without peers or for narrow B.
-std::vector<std::pair<int, int>> col_panels(int n, int world) {
+// Column panels of B (the same schedule as matrixflash_pro_b200.distributed.col_panels): a
+// leading panel of a tenth of the columns in whole 256-column tiles and at most 128 MB of B (its
+// broadcast is the only one nothing hides); then, while the rest of B is over 512 MB and over four
+// times the last panel, a panel twice as wide as the last (a panel's GEMM takes 2 * rows * k FLOP
+// per column, its transfer 4 * k bytes, so a doubled panel arrives during the previous GEMM);
+// then the rest. One panel without peers or for narrow B.
+std::vector<std::pair<int, int>> col_panels(int n, int world, long long k) {
     std::vector<std::pair<int, int>> p;
     if (world <= 1 || n <= 2 * kPanelTile) {
         p.emplace_back(0, n);
         return p;
     }
-    const int first = std::max(kPanelTile, static_cast<int>(n * 0.1) / kPanelTile * kPanelTile);
+    int first = std::max(kPanelTile, static_cast<int>(n * 0.1) / kPanelTile * kPanelTile);
+    if (k > 0)
+        first = std::min<long long>(first, std::max<long long>(kPanelTile, (128LL << 20) / (4 * k) / kPanelTile * kPanelTile));
     if (first >= n) {
         p.emplace_back(0, n);
         return p;
     }
     p.emplace_back(0, first);
-    p.emplace_back(first, n);
+    long long width = first, start = first;
+    while (4 * k * (n - start) > (512LL << 20) && n - start > 4 * width) {
+        width *= 2;
+        p.emplace_back(static_cast<int>(start), static_cast<int>(start + width));
+        start += width;
+    }
+    p.emplace_back(static_cast<int>(start), n);
     return p;
 }
 
@@ -166,7 +179,7 @@ mfb_status_t run_multi(const mfb_row_block* blocks, int count, int root, const m
     }
     if (d.m == 0 || d.n == 0) return MFB_OK;
     const bool with_bias = d.epilogue != MFB_EPILOGUE_NONE;
-    const auto panels = col_panels(d.n, count);
+    const auto panels = col_panels(d.n, count, d.k);
     const size_t b_floats = static_cast<size_t>(d.k) * static_cast<size_t>(d.n);
     std::vector<DevState*> st(count, nullptr);
     for (int r = 0; r < count; ++r) {

@@ -67,18 +67,20 @@ def row_partition(m: int, world: int, rank: int) -> Tuple[int, int]:
 
 
 def col_panels(n: int, world: int, k: int = 0, first_fraction: float = 0.1, tile: int = 256,
-               max_first_bytes: int = 128 << 20, stop_ratio: int = 4) -> List[Tuple[int, int]]:
+               max_first_bytes: int = 128 << 20, max_rest_bytes: int = 512 << 20,
+               stop_ratio: int = 4) -> List[Tuple[int, int]]:
     """Column panels for the broadcast/GEMM pipeline. A single panel without peers.
 
     The first panel's broadcast is the only transfer nothing hides, so it is small: a tenth of
     the columns in whole 256-column tiles (measured best on 2 B200s for the linear layer,
-    n = 11008: 1024 columns), and at most max_first_bytes of B. Each later panel must arrive
-    while the GEMM of the one before runs; a panel's GEMM takes 2 * m_local * k FLOP per
-    column and its transfer 4 * k bytes per column, so with m_local in the thousands a panel
-    twice as wide as the previous one arrives in time. Panels therefore double until the
-    rest of B is at most stop_ratio times the last panel, and the rest is the final panel.
-    For n = 32768, k = 32768 (a 4.3 GB B): 1024, 2048, 4096, 8192, 17408 columns, where two
-    panels (3072 + 29696) would leave the GPUs waiting for the 3.9 GB second one."""
+    n = 11008: 1024 columns, then the rest), and at most max_first_bytes of B. Each later panel
+    must arrive while the GEMM of the one before runs; a panel's GEMM takes 2 * m_local * k FLOP
+    per column and its transfer 4 * k bytes per column, so with m_local in the thousands a panel
+    twice as wide as the previous one arrives in time. While the rest of B is larger than
+    max_rest_bytes and than stop_ratio times the last panel, the next panel is twice the last;
+    the rest is the final panel. For n = 32768, k = 32768 (a 4.3 GB B): 1024, 2048, 4096, 8192,
+    17408 columns, where a tenth plus the rest (3072 + 29696) would leave the GPUs waiting for a
+    3.9 GB second panel. The linear layer (a 163 MB rest) keeps its two panels."""
     if world <= 1 or n <= 2 * tile:
         return [(0, n)]
     first = max(tile, int(n * first_fraction) // tile * tile)
@@ -88,7 +90,7 @@ def col_panels(n: int, world: int, k: int = 0, first_fraction: float = 0.1, tile
         return [(0, n)]
     panels = [(0, first)]
     width, start = first, first
-    while n - start > stop_ratio * width:
+    while 4 * k * (n - start) > max_rest_bytes and n - start > stop_ratio * width:
         width *= 2
         panels.append((start, start + width))
         start += width

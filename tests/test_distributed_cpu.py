@@ -29,7 +29,7 @@ def test_row_partition_covers_rows_once():
 
 def test_col_panels():
     assert col_panels(11008, 1) == [(0, 11008)]
-    assert col_panels(11008, 8, 4096) == [(0, 1024), (1024, 3072), (3072, 11008)]
+    assert col_panels(11008, 8, 4096) == [(0, 1024), (1024, 11008)]  # the linear layer: a 163 MB rest
     # a 4.3 GB B: a 128 MB first panel, then panels doubling while the rest is > 4x the last
     assert col_panels(32768, 8, 32768) == [(0, 1024), (1024, 3072), (3072, 7168), (7168, 15360), (15360, 32768)]
     assert col_panels(300, 4) == [(0, 300)]
@@ -38,13 +38,16 @@ def test_col_panels():
         assert p[0][0] == 0 and p[-1][1] == n and all(a < b for a, b in p) and p[0][1] % 256 == 0
         assert all(x[1] == y[0] for x, y in zip(p, p[1:]))
         assert all(b1 - b0 <= 2 * (a1 - a0) for (a0, a1), (b0, b1) in zip(p[:-2], p[1:-1]))
+        assert len(p) <= 2 or 4 * k * (p[-2][0] - p[-3][1] + (n - p[-2][0])) > 512 << 20
         if k:
             assert p[0][1] - p[0][0] == 256 or (p[0][1] - p[0][0]) * 4 * k <= 128 << 20
 
 
 def test_schedule_sm_limits():
     s = schedule(11008, 4, 32, 148, 4096)
-    assert s.sm_limits == [116, 116, None] and len(s.panels) == 3
+    assert s.sm_limits == [116, None] and len(s.panels) == 2
+    s5 = schedule(32768, 8, 32, 148, 32768)
+    assert s5.sm_limits == [116, 116, 116, 116, None] and len(s5.panels) == 5
     s1 = schedule(11008, 1, 16, 148)
     assert s1.panels == [(0, 11008)] and s1.sm_limits == [None]
 
