@@ -829,7 +829,9 @@ def main():
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_used, "unit": "TFLOP/s",
                 "frac": (achieved / peak_used) if achieved else None, "traffic": traffic,
                 "kernel": "tc_pair_kernel / tc_persistent_kernel (tcgen05 kind::tf32, "
-                          + ("3xTF32" if strict else "1xTF32") + ")",
+                          + ("3xTF32" if strict else "1xTF32") + ")"
+                          + (" + streamk_reduce_kernel (the last tiles share K among the SMs; the timed GEMM "
+                             "phase includes this fix-up)" if op.plan.stream_k and world == 1 else ""),
                 "peak_basis": f"{basis}/{int(passes)} of {peak_src} MEASURED_PEAKS.json "
                               f"({'sustained: long steps hit the power cap' if long_run else 'burst: short steps'}; "
                               "TF32 = bf16/2, strict = 3 TF32 passes)",
