@@ -244,6 +244,25 @@ class RowSplitGemm:
                                for (n0, n1) in self.sched.panels]
         # GEMM kernel time of the last step per panel, when events are requested.
         self.kernel_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
+        # SMs are left to NCCL only while broadcasts run: a panel's GEMM is capped (sched.sm_limits)
+        # until a step shows it started after the last panel had arrived (see _update_caps).
+        self.capped = [lim is not None for lim in self.sched.sm_limits]
+        self._gemm_start = [torch.cuda.Event(enable_timing=True) for _ in self.sched.panels]
+        self._arrived_last = torch.cuda.Event(enable_timing=True)
+        self._recorded = False
+
+    def _update_caps(self) -> None:
+        """From the previous step's events: a panel whose GEMM started after the last panel had
+        arrived (all broadcasts done) runs on every SM from now on; one that started before stays
+        capped. The first panel always overlaps the later broadcasts. Local to this rank (no
+        collective), and only once the previous step's events have completed."""
+        if not self._recorded or not self._arrived_last.query():
+            return
+        for i in range(len(self.sched.panels) - 1):
+            start = self._gemm_start[i]
+            # started at least 50 us after the last panel landed: no broadcast left to make room for
+            if self.capped[i] and start.query() and start.elapsed_time(self._arrived_last) <= -0.05:
+                self.capped[i] = False
 
     def __call__(self, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, alpha: float = 1.0, beta: float = 0.0,
                  time_kernels: bool = False) -> None:
@@ -289,15 +308,20 @@ class RowSplitGemm:
             # the panel's B prepass, on whichever stream is current (the side stream for
             # panels after the first: it overlaps the previous panel's GEMM)
             n0, n1 = panel
+            if i == len(self.sched.panels) - 1:
+                self._arrived_last.record(torch.cuda.current_stream())  # every broadcast has landed
             plan.prepare_cols(_stream_handle(), self.panel_bufs[i].data_ptr(), n1 - n0, n0, n1)
 
         def panel_gemm(i, panel, sm_limit):
             n0, n1 = panel
-            plan.set_sm_limit(sm_limit)
+            plan.set_sm_limit(sm_limit if self.capped[i] else None)
+            self._gemm_start[i].record(torch.cuda.current_stream())
             timed(lambda: plan.multiply_cols(stream, a0, c0, alpha, beta, n0, n1))
 
+        self._update_caps()
         run_schedule(self.sched, lambda i: self.panel_bufs[i], pack, panel_gemm, self.group, self.src,
                      before_wait=prepare_a, prepare_panel=prepare_panel, side=self.side)
+        self._recorded = True
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step: on one GPU the operand prepass (hi/lo split, or TF32
