@@ -868,7 +868,9 @@ def main():
                               f"{FLUSH_BYTES >> 20} MiB write between steps, each step timed alone by CUDA "
                               "events" if flush else
                               f"step footprint {footprint / 2**20:.0f} MiB, larger than L2 (126 MB) every step"),
-                       "global_batch": m * world, "seq_len": None},
+                       "global_batch": m * world, "seq_len": None,
+                       "b_panels": op.sched.panels if world > 1 else None,
+                       "panels_capped_at_end": ([i for i, c in enumerate(op.capped) if c] if world > 1 else None)},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": op.launches_per_step() * args.steps, "clocks": clk, "check": check_line,
         }
