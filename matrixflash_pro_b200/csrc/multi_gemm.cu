@@ -15,7 +15,9 @@
 //   * Each GPU splits its A block into TF32 planes on its compute stream while B is in flight,
 //     splits each panel into the plan's B planes on a second stream as soon as it has arrived,
 //     and multiplies C[:, n0:n1] on the compute stream (mfb_plan_multiply_cols). GEMMs that
-//     run while later panels are still broadcasting leave kCommSms SMs to NCCL.
+//     run while later panels are still broadcasting leave kCommSms SMs to NCCL: every panel but
+//     the last at first, then only those whose GEMM started before the last panel had landed
+//     in the previous call with the same schedule (timed events).
 //   * Blocking: work already queued on the devices finishes first, and the call returns when
 //     every GPU is done, like the reference's scheduler.
 #include "mfb_internal.h"
@@ -78,7 +80,30 @@ struct DevState {
     std::vector<cudaEvent_t> arrived;   // per panel, on the communication stream
     std::vector<cudaEvent_t> prepared;  // per panel, on the prepare stream
     cudaEvent_t bias_ready = nullptr;
+    // Adaptive SM cap (timed events): when the last panel landed, when each panel's GEMM started,
+    // and which panels still leave SMs to NCCL, for the panel schedule of the last call.
+    cudaEvent_t last_arrived = nullptr;
+    std::vector<cudaEvent_t> gemm_start;
+    std::vector<std::pair<int, int>> schedule;
+    std::vector<char> capped;
+    bool recorded = false;
 };
+
+// A panel's GEMM that started at least 50 us after the last panel landed (previous call) runs on
+// every SM from now on; the others keep leaving kCommSms SMs to NCCL.
+void update_caps(DevState& s) {
+    if (!s.recorded || cudaEventQuery(s.last_arrived) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    for (size_t i = 0; i + 1 < s.schedule.size(); ++i) {
+        float ms = 0.0f;
+        if (s.capped[i] && cudaEventQuery(s.gemm_start[i]) == cudaSuccess &&
+            cudaEventElapsedTime(&ms, s.gemm_start[i], s.last_arrived) == cudaSuccess && ms <= -0.05f)
+            s.capped[i] = 0;
+    }
+    cudaGetLastError();
+}
 
 std::mutex g_multi_mutex;  // one call at a time: the per-device state is shared
 std::map<int, std::unique_ptr<DevState>> g_states;
@@ -111,14 +136,17 @@ mfb_status_t device_state(int device, size_t panel_count, size_t b_floats, size_
         MFB_CUDA_TRY(cudaStreamCreateWithFlags(&slot->compute, cudaStreamNonBlocking), "multi-GPU compute stream");
         MFB_CUDA_TRY(cudaStreamCreateWithFlags(&slot->prepare, cudaStreamNonBlocking), "multi-GPU prepare stream");
         MFB_CUDA_TRY(cudaEventCreateWithFlags(&slot->bias_ready, cudaEventDisableTiming), "event");
+        MFB_CUDA_TRY(cudaEventCreate(&slot->last_arrived), "event");
     }
     DevState* st = slot.get();
     while (st->arrived.size() < panel_count) {
-        cudaEvent_t a = nullptr, p = nullptr;
+        cudaEvent_t a = nullptr, p = nullptr, g = nullptr;
         MFB_CUDA_TRY(cudaEventCreateWithFlags(&a, cudaEventDisableTiming), "event");
         MFB_CUDA_TRY(cudaEventCreateWithFlags(&p, cudaEventDisableTiming), "event");
+        MFB_CUDA_TRY(cudaEventCreate(&g), "event");
         st->arrived.push_back(a);
         st->prepared.push_back(p);
+        st->gemm_start.push_back(g);
     }
     MFB_TRY(grow(&st->panels, &st->panel_floats, std::max<size_t>(b_floats, 1)));
     if (bias_n) MFB_TRY(grow(&st->bias, &st->bias_floats, bias_n));
@@ -199,6 +227,17 @@ mfb_status_t run_multi(const mfb_row_block* blocks, int count, int root, const m
         return read_and_clear_status(nullptr);
     }
 
+    for (int r = 0; r < count; ++r) {
+        DevState& s = *st[r];
+        if (s.schedule != panels) {  // a new panel schedule: cap every panel but the last again
+            s.schedule = panels;
+            s.capped.assign(panels.size(), 1);
+            s.capped.back() = 0;
+            s.recorded = false;
+        } else {
+            update_caps(s);
+        }
+    }
     std::vector<cudaStream_t> comm;
     MFB_TRY(nccl_streams(devices, &comm));
     // Root: each panel packed contiguous on its communication stream, ahead of its broadcast.
@@ -231,6 +270,7 @@ mfb_status_t run_multi(const mfb_row_block* blocks, int count, int root, const m
         for (int r = 0; r < count; ++r) {
             MFB_CUDA_TRY(cudaSetDevice(devices[r]), "cudaSetDevice");
             MFB_CUDA_TRY(cudaEventRecord(st[r]->arrived[i], comm[r]), "event record");
+            if (i + 1 == panels.size()) MFB_CUDA_TRY(cudaEventRecord(st[r]->last_arrived, comm[r]), "event record");
         }
     }
     // Per GPU: A's planes while B is in flight, each panel's planes as it lands, its GEMM.
@@ -253,11 +293,13 @@ mfb_status_t run_multi(const mfb_row_block* blocks, int count, int root, const m
         for (size_t i = 0; i < panels.size(); ++i) {
             const int n0 = panels[i].first, n1 = panels[i].second;
             MFB_CUDA_TRY(cudaStreamWaitEvent(s.compute, s.prepared[i], 0), "wait planes");
-            MFB_TRY(mfb_plan_set_sm_limit(s.plan, i + 1 < panels.size() ? std::max(1, sms - kCommSms) : 0));
+            MFB_TRY(mfb_plan_set_sm_limit(s.plan, s.capped[i] ? std::max(1, sms - kCommSms) : 0));
+            MFB_CUDA_TRY(cudaEventRecord(s.gemm_start[i], s.compute), "event record");
             MFB_TRY(mfb_plan_multiply_cols(s.plan, cs, blk.a, blk.c, d.alpha, d.beta, with_bias ? s.bias : nullptr,
                                            n0, n1));
         }
     }
+    for (int r = 0; r < count; ++r) st[r]->recorded = true;
     mfb_status_t result = MFB_OK;
     for (int r = 0; r < count; ++r) {
         MFB_CUDA_TRY(cudaSetDevice(devices[r]), "cudaSetDevice");
