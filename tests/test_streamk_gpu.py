@@ -174,3 +174,38 @@ def test_one_shot_and_batched_calls_take_the_split_path():
         ref32, ref64 = _ref(a[i], b[i], np.zeros((m, n), np.float32), 1.0, 0.0)
         _gate(got[i], ref32, ref64, a[i], b[i], FP32, f"batch entry {i}")
     assert mf.device_status(0) == 0
+
+
+def test_stream_k_plan_replays_in_a_cuda_graph():
+    """A plan whose last tiles share K (GEMM + fix-up, both launched programmatically) captures into a
+    CUDA graph; replays give the eager bits and read updated inputs."""
+    m = n = 512
+    k = 16384
+    g = torch.Generator(device="cuda").manual_seed(21)
+    A = torch.randn((m, k), device="cuda", generator=g)
+    B = torch.randn((k, n), device="cuda", generator=g)
+    C0 = torch.randn((m, n), device="cuda", generator=g)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        plan = mf.GemmPlan(m, n, k)
+        assert plan.info().stream_k_tiles > 0
+        eager = C0.clone()
+        plan.execute(A, B, eager, 0.5, 1.0)
+        C = C0.clone()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            plan.execute(A, B, C, 0.5, 1.0)
+        C.copy_(C0)
+        graph.replay()
+    side.synchronize()
+    assert torch.equal(C, eager)
+    with torch.cuda.stream(side):
+        B.mul_(2.0)
+        C.copy_(C0)
+        graph.replay()
+        want = C0.clone()
+        plan.execute(A, B, want, 0.5, 1.0)
+    side.synchronize()
+    assert torch.equal(C, want)
+    mf.sync()
