@@ -704,6 +704,16 @@ def main():
         op(A, B, C, alpha, beta)
     torch.cuda.synchronize()
     mf.sync()
+    # one more warm-up step, timed, to tell short steps from long ones (see the timed loop)
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record()
+    op(A, B, C, alpha, beta)
+    w1.record()
+    torch.cuda.synchronize()
+    t_warm = torch.tensor([w0.elapsed_time(w1)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_warm, op=dist.ReduceOp.MAX)  # every rank takes the same branch
+    short_steps = float(t_warm.item()) < 1.0
 
     # ---------------------------------------------------------------- timed region (device)
     # Bytes one step touches: A, B, C (read and written) and the operand planes of the prepass.
@@ -712,30 +722,36 @@ def main():
     flush = footprint < 2 * L2_BYTES  # otherwise the inputs exceed L2 every step
     flush_buf = torch.empty(FLUSH_BYTES // 4, device="cuda") if flush else None
     stream = torch.cuda.current_stream()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kernel_ms = 0.0
     step_events = []
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
-        e_start.record(stream)
         kernel_records = []
         for _ in range(args.steps):
+            # The GEMM kernels' own time, for the roofline, comes from CUDA events around each
+            # GEMM launch. An event between the prepass and the GEMM keeps the GEMM from
+            # launching programmatically behind the prepass: measured 4-8% of a 2048^3 step,
+            # noise on a 3 ms step. Short steps (under 1 ms) therefore run clean and each is
+            # followed by an untimed twin that carries the events, under the same flush,
+            # clocks and power state; long steps carry the events themselves, since a twin per
+            # step would double their power draw and bring on the power cap. Every timed step
+            # is bracketed by its own events and `value` sums those.
             if flush:
-                # a write larger than L2 between steps; each step is timed alone
-                flush_buf.zero_()
-                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s0.record(stream)
-            op(A, B, C, alpha, beta, time_kernels=True)
-            if flush:
-                s1.record(stream)
-                step_events.append((s0, s1))
+                flush_buf.zero_()  # a write larger than L2 before each step
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            op(A, B, C, alpha, beta, time_kernels=not short_steps)
+            s1.record(stream)
+            step_events.append((s0, s1))
+            if short_steps:
+                if flush:
+                    flush_buf.zero_()
+                op(A, B, C, alpha, beta, time_kernels=True)
             kernel_records.extend(op.kernel_events)
-        e_end.record(stream)
         torch.cuda.synchronize()
         barrier()
-    elapsed_ms = (sum(a.elapsed_time(b) for a, b in step_events) if flush
-                  else e_start.elapsed_time(e_end))
+    elapsed_ms = sum(a.elapsed_time(b) for a, b in step_events)
     kernel_ms = sum(a.elapsed_time(b) for a, b in kernel_records)
     mf.sync()  # raises on a device-side timeout
 
@@ -837,6 +853,9 @@ def main():
                               "TF32 = bf16/2, strict = 3 TF32 passes)",
                 "peak_burst": peak_burst, "peak_sustained": peak_sust,
                 "kernel_ms_per_launch": kernel_ms / max(1, launches_gemm),
+                "kernel_timing": ("CUDA events around each GEMM launch of an untimed twin that follows every "
+                                  "timed step (steps under 1 ms)" if short_steps else
+                                  "CUDA events around each GEMM launch of the timed steps"),
                 "flops_per_launch": gemm_flops / max(1, launches_gemm)}
     if rank == 0:
         roofline.update(tf32_mma_fields(mf, local, achieved, strict))
@@ -867,7 +886,8 @@ def main():
                        "l2": (f"step footprint {footprint / 2**20:.0f} MiB < 2 x L2: L2 flushed by a "
                               f"{FLUSH_BYTES >> 20} MiB write between steps, each step timed alone by CUDA "
                               "events" if flush else
-                              f"step footprint {footprint / 2**20:.0f} MiB, larger than L2 (126 MB) every step"),
+                              f"step footprint {footprint / 2**20:.0f} MiB, larger than L2 (126 MB) every step; "
+                              "each step timed alone by CUDA events"),
                        "global_batch": m * world, "seq_len": None,
                        "b_panels": op.sched.panels if world > 1 else None,
                        "panels_capped_at_end": ([i for i, c in enumerate(op.capped) if c] if world > 1 else None)},
