@@ -34,15 +34,22 @@ struct GemmTcParams {
 };
 
 // FP32 sums of a stream-K share: slot `slot` holds one tile of ROWS x BN floats, row-major;
-// CTA `rank` of an SM pair writes rows [128 rank, 128 rank + 128).
+// CTA `rank` of an SM pair writes rows [128 rank, 128 rank + 128). Slots start 256-byte
+// aligned and COUNT-column groups start at multiples of COUNT, so 8-column groups take
+// whole-sector stores.
 template <int ROWS, int BN, int COUNT>
 __device__ __forceinline__ void store_partial_rows(const GemmTcParams& p, int slot, int rank, int row_in_tile,
                                                    int col0_in_tile, const float* v) {
     float* dst = p.partials + static_cast<long long>(slot) * (ROWS * BN) +
                  static_cast<long long>(rank * kTcBM + row_in_tile) * BN + col0_in_tile;
+    if constexpr (COUNT % 8 == 0) {
 #pragma unroll
-    for (int j = 0; j < COUNT / 4; ++j)
-        reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        for (int j = 0; j < COUNT / 8; ++j) st_global_v8(dst + 8 * j, v + 8 * j);
+    } else {
+#pragma unroll
+        for (int j = 0; j < COUNT / 4; ++j)
+            reinterpret_cast<float4*>(dst)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
 }
 
 constexpr int kBK = 32;  // 32 fp32 = 128 bytes of K per stage: one swizzle row
@@ -133,7 +140,11 @@ struct GemmProblem {
         store_partial_rows<kTcBM, BN, COUNT>(p, slot, rank, row_in_tile, col0_in_tile, v);
     }
 
-    // Writes COUNT consecutive outputs of one row: o = epilogue(alpha * acc + beta * C).
+    // Writes COUNT consecutive outputs of one row: o = epilogue(alpha * acc + beta * C). Each
+    // thread writes its own row. Where the row segment is 32-byte aligned it goes out in
+    // whole-sector (256-bit) stores: 2048^3 GEMM 86.0 -> 84.0 us against 128-bit stores.
+    // (Staging 32 x 32 blocks through shared memory for 4-row x 128-byte stores was slower
+    // inside the GEMM: 87 -> 102 us.)
     template <int COUNT>
     __device__ static void store(const Params& p, const Tile& t, int row_in_tile, int col0_in_tile, const float* v) {
         const int row = t.m0 + row_in_tile;
@@ -146,22 +157,31 @@ struct GemmProblem {
 #pragma unroll
                 for (int j = 0; j < COUNT / 4; ++j) cin[j] = *reinterpret_cast<const float4*>(crow + col0 + 4 * j);
             }
+            float o[COUNT];
 #pragma unroll
             for (int j = 0; j < COUNT / 4; ++j) {
-                float o[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) o[e] = p.alpha * v[4 * j + e];
+                for (int e = 0; e < 4; ++e) o[4 * j + e] = p.alpha * v[4 * j + e];
                 if (p.beta != 0.0f) {
-                    o[0] = fmaf(p.beta, cin[j].x, o[0]);
-                    o[1] = fmaf(p.beta, cin[j].y, o[1]);
-                    o[2] = fmaf(p.beta, cin[j].z, o[2]);
-                    o[3] = fmaf(p.beta, cin[j].w, o[3]);
+                    o[4 * j + 0] = fmaf(p.beta, cin[j].x, o[4 * j + 0]);
+                    o[4 * j + 1] = fmaf(p.beta, cin[j].y, o[4 * j + 1]);
+                    o[4 * j + 2] = fmaf(p.beta, cin[j].z, o[4 * j + 2]);
+                    o[4 * j + 3] = fmaf(p.beta, cin[j].w, o[4 * j + 3]);
                 }
                 if (p.epilogue) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) o[e] = apply_epilogue_op(o[e], p.bias, col0 + 4 * j + e, p.epilogue);
+                    for (int e = 0; e < 4; ++e)
+                        o[4 * j + e] = apply_epilogue_op(o[4 * j + e], p.bias, col0 + 4 * j + e, p.epilogue);
                 }
-                *reinterpret_cast<float4*>(crow + col0 + 4 * j) = make_float4(o[0], o[1], o[2], o[3]);
+            }
+            if (COUNT % 8 == 0 && (reinterpret_cast<uintptr_t>(crow + col0) & 31) == 0) {
+#pragma unroll
+                for (int j = 0; j < COUNT / 8; ++j) st_global_v8(crow + col0 + 8 * j, o + 8 * j);
+            } else {
+#pragma unroll
+                for (int j = 0; j < COUNT / 4; ++j)
+                    *reinterpret_cast<float4*>(crow + col0 + 4 * j) =
+                        make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
             }
         } else {
 #pragma unroll
